@@ -75,17 +75,22 @@ def preset(name: str) -> ModelConfig:
 
     * ``cfg1``: one DeltaNet layer + one full-attention layer at 9B shapes, vocab 1024.
     * ``cfg2``: the full 32-layer 9B-shaped model with the real vocab (248320).
-    * ``small``: the 9B layer pattern at reduced widths, for fast CPU checks.
+    * ``small``: the 9B layer pattern at reduced widths, for fast CPU checks. Its widths
+      keep every reference GEMV either single-threaded or on all 8 pool threads: the
+      reference's WorkerPool (xq_gemv_w4a16_neon.cpp:145-182) can hang when a call uses
+      more than one but fewer than all of its threads. Like the 9B shapes it keeps
+      heads * head_dim == hidden and value heads * 128 <= hidden, which the reference's
+      scratch sizing assumes (custom_model.cpp:478-498).
     """
     if name == "cfg1":
         return ModelConfig(vocab_size=1024, layer_types=["linear_attention", "full_attention"])
     if name == "cfg2":
         return qwen35_9b()
     if name == "small":
-        return ModelConfig(hidden_size=1024, intermediate_size=2048, vocab_size=2048,
-                           num_attention_heads=4, num_key_value_heads=1, head_dim=256,
+        return ModelConfig(hidden_size=2048, intermediate_size=2048, vocab_size=4096,
+                           num_attention_heads=8, num_key_value_heads=4, head_dim=256,
                            linear_key_head_dim=128, linear_value_head_dim=128,
-                           linear_num_key_heads=2, linear_num_value_heads=4,
+                           linear_num_key_heads=8, linear_num_value_heads=16,
                            layer_types=["linear_attention", "linear_attention",
                                         "linear_attention", "full_attention"])
     raise ValueError(f"unknown preset {name!r}")
