@@ -1,0 +1,81 @@
+/* xq_kernels.h: kernel-level C ABI of libxqwen35.so.
+ *
+ * The reference exposes its kernels as C++ functions over xq::kernels::QuantizedMatrix
+ * (customlib/kernels/kernels.hpp:11-53). A host binding them through an FFI needs plain C,
+ * so each entry point below takes plain pointers and sizes. Pointers named *_dev are CUDA
+ * device pointers; `stream` is a cudaStream_t passed as void* (NULL = the legacy default
+ * stream). Entry points return 0 on success and a negative xq_status value on error;
+ * xqk_last_error() returns the message of the last failure on the calling thread.
+ */
+#ifndef XQ_KERNELS_H_
+#define XQ_KERNELS_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XQK_API __attribute__((visibility("default")))
+
+/* A W4A16 matrix resident in device memory in the B200 row layout: each row is its
+ * nibbles (reference order) followed by that row's group metadata, 16-byte aligned, so one
+ * contiguous bulk copy moves a block of rows with their scales. */
+typedef struct xqk_matrix xqk_matrix;
+
+XQK_API const char* xqk_last_error(void);
+
+/* Upload a matrix given in the reference's QuantizedMatrix fields (kernels.hpp:11-21,
+ * XQ4 payload order custom_model.cpp:218-262): packed rows*ceil(cols/2) bytes (even column
+ * in the low nibble), fp32 scales and zeros rows*ceil(cols/group) each; version 1 means
+ * (code - zero) * scale, version 2 means code * scale + zero. Host pointers. */
+XQK_API int xqk_matrix_create(const uint8_t* packed, const float* scales, const float* zeros, int rows,
+                              int cols, int group_size, int version, int device, xqk_matrix** out);
+XQK_API void xqk_matrix_destroy(xqk_matrix* m);
+/* rows, cols, device bytes, row stride, layout kind (0 fp16 scale with zero 8, 1 fp32
+ * scale/offset pairs, 2 generic), and whether the fused fast kernel serves this shape. */
+XQK_API int xqk_matrix_info(const xqk_matrix* m, int* rows, int* cols, size_t* device_bytes, int* row_stride,
+                            int* layout_kind, int* fast_path);
+
+/* y = W x, fp32 in/out, device pointers (gemvW4A16Neon, xq_gemv_w4a16_neon.cpp:259). */
+XQK_API int xqk_gemv_w4a16(const xqk_matrix* m, const float* x_dev, float* y_dev, void* stream);
+/* Same with host buffers: copies x in, runs, copies y out, synchronises. */
+XQK_API int xqk_gemv_w4a16_host(const xqk_matrix* m, const float* x_host, float* y_host);
+/* argmax_r (W x)[r], ties to the lowest index (gemvW4A16ArgmaxNeon,
+ * xq_gemv_w4a16_neon.cpp:293-348); writes the index and the value to device memory. Uses
+ * per-matrix scratch allocated at creation: calls on one matrix must not overlap. */
+XQK_API int xqk_gemv_w4a16_argmax(const xqk_matrix* m, const float* x_dev, int32_t* index_dev,
+                                  float* value_dev, void* stream);
+
+/* y = x * rsqrt(mean(x^2) + eps) * w (rmsnormReference, ref_rmsnorm.cpp:8-17). */
+XQK_API int xqk_rmsnorm(const float* x_dev, const float* w_dev, int n, float eps, float* y_dev, void* stream);
+
+/* One Gated-DeltaNet decode step for all value heads, the fused form the runtime uses:
+ * l2-normalise q and k per key head (custom_model.cpp:315-327), beta = sigmoid(b),
+ * g = -exp(A_log) * softplus(a + dt_bias) (custom_model.cpp:1075-1082), then the
+ * gated delta rule per head (gatedDeltaDecodeReference, ref_delta.cpp:8-41).
+ * conv_dev: [2*nk*dk + nv*dv] = q | k | v after conv+SiLU; ab_dev: [a (nv) | b (nv)];
+ * state_dev: [nv][dk][dv] fp32, updated in place; out_dev: [nv*dv]. dk = dv = 128. */
+XQK_API int xqk_gated_delta_step(const float* conv_dev, const float* ab_dev, const float* a_log_dev,
+                                 const float* dt_bias_dev, float* state_dev, float* out_dev, int nk, int nv,
+                                 int dk, int dv, void* stream);
+
+/* One full-attention decode step for one layer, the fused form the runtime uses:
+ * per-head [query|gate] split of q_proj rows (custom_model.cpp:740-753), head RMSNorm on q
+ * and k (applyHeadRms, :301-313), partial NeoX RoPE (applyRopeVector, :351-370), KV append
+ * at `position` (appendKv, :673-733, layout [t][kv_head][head_dim]), GQA softmax attention
+ * over positions 0..position (:871-928) and the sigmoid output gate (:944-946).
+ * qkv_dev: [2*nq*hd | nkv*hd | nkv*hd] raw projections; q_norm/k_norm with +1 applied;
+ * k_cache/v_cache: [capacity][nkv][hd], fp32 (kv_fp16 = 0) or fp16 (kv_fp16 = 1).
+ * out_dev: [nq*hd]. Uses internal scratch sized for `capacity`; calls must not overlap. */
+XQK_API int xqk_attention_step(const float* qkv_dev, const float* q_norm_dev, const float* k_norm_dev,
+                               void* k_cache_dev, void* v_cache_dev, int kv_fp16, int capacity, int position,
+                               int nq, int nkv, int hd, int rotary_dim, float theta, float eps, float* out_dev,
+                               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XQ_KERNELS_H_ */

@@ -1,0 +1,123 @@
+/* xqwen35.h: public C ABI of the B200 decode library (libxqwen35.so).
+ *
+ * Drop-in for the reference header customlib/include/xqwen35.h: every type, enum value and
+ * entry point below has the same name, layout and meaning as xqwen35.h:19-77 of the
+ * reference, so a host that compiled against that header links against this library
+ * unchanged. The work behind it runs on an NVIDIA B200 (sm_100a): weights, KV cache and
+ * recurrent state live in HBM and each decode step is one CUDA graph.
+ *
+ * Additions (not in the reference): xq_cuda_options + xq_create_cuda, to pick the device
+ * and KV-cache precision; everything else is the reference interface.
+ */
+#ifndef XQWEN35_H_
+#define XQWEN35_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define XQ_API __attribute__((visibility("default")))
+
+/* Opaque session handle (reference xqwen35.h:19). */
+typedef struct xq_session xq_session;
+
+/* Status codes (reference xqwen35.h:21-28). */
+typedef enum xq_status {
+    XQ_OK = 0,
+    XQ_ERR_INVALID_ARGUMENT = -1,
+    XQ_ERR_NOT_READY = -2,
+    XQ_ERR_MODEL = -3,
+    XQ_ERR_RUNTIME = -4,
+    XQ_ERR_BUFFER_TOO_SMALL = -5
+} xq_status;
+
+/* Creation options (reference xqwen35.h:30-40). backend: any string is accepted and the
+ * CUDA path always runs (there is no CPU fallback); threads, quant_bits, group_size,
+ * enable_autotune and telemetry_path are accepted and ignored as in the reference's custom
+ * path; max_context_tokens sizes the initial KV cache (it grows on demand);
+ * use_mnn_fallback is accepted and ignored (the MNN engine is not part of this library). */
+typedef struct xq_options {
+    size_t struct_size;
+    const char* backend;
+    int threads;
+    int quant_bits;
+    int group_size;
+    int max_context_tokens;
+    int enable_autotune;
+    int use_mnn_fallback;
+    const char* telemetry_path;
+} xq_options;
+
+/* Metrics (reference xqwen35.h:42-58). Copies are bounded by the caller's struct_size. */
+typedef struct xq_metrics {
+    size_t struct_size;
+    uint64_t prompt_tokens;
+    uint64_t generated_tokens;
+    double load_ms;
+    double prefill_ms;
+    double first_token_ms;
+    double decode_total_ms;
+    double total_generate_ms;
+    double prefill_tokens_per_second;
+    double decode_tokens_per_second;
+    uint64_t rss_kb;
+    uint64_t pss_kb;
+    char backend[64];
+    char selected_kernels[512];
+    char error[256];
+} xq_metrics;
+
+/* Reference xqwen35.h:60 (session.cpp:620-632): load a model directory onto the GPU. */
+XQ_API xq_status xq_create(const char* model_dir, const xq_options* options, xq_session** out_session);
+/* Reference xqwen35.h:61 (session.cpp:634-636). */
+XQ_API void xq_destroy(xq_session* session);
+/* Reference xqwen35.h:62 (session.cpp:304-342): token-serial prefill, no logits. */
+XQ_API xq_status xq_prefill(xq_session* session, const int32_t* token_ids, size_t n_tokens, xq_metrics* out_metrics);
+/* Reference xqwen35.h:63 (session.cpp:344-383): greedy sample, then forward that token. */
+XQ_API xq_status xq_decode_one(xq_session* session, int32_t* out_token_id, xq_metrics* out_metrics);
+/* Reference xqwen35.h:64-70 (session.cpp:385-421): prefill + max_new_tokens decodes. */
+XQ_API xq_status xq_generate(xq_session* session,
+                             const int32_t* token_ids,
+                             size_t n_tokens,
+                             size_t max_new_tokens,
+                             int32_t* output_buffer,
+                             size_t output_capacity,
+                             xq_metrics* out_metrics);
+/* Reference xqwen35.h:71 (session.cpp:505-525). */
+XQ_API xq_status xq_reset(xq_session* session);
+/* Reference xqwen35.h:72. */
+XQ_API xq_status xq_get_last_metrics(xq_session* session, xq_metrics* out_metrics);
+/* Reference xqwen35.h:73-75: JSON into caller buffers, XQ_ERR_BUFFER_TOO_SMALL if short. */
+XQ_API xq_status xq_get_backend_info(xq_session* session, char* json_out, size_t json_capacity);
+XQ_API xq_status xq_get_kernel_trace_json(xq_session* session, char* json_out, size_t json_capacity);
+XQ_API xq_status xq_get_debug_json(xq_session* session, char* json_out, size_t json_capacity);
+/* Reference xqwen35.h:76 (custom_model.cpp:1438-1447): post-final-norm hidden state. */
+XQ_API xq_status xq_get_hidden_state(xq_session* session, float* out_values, size_t value_capacity, size_t* out_size);
+/* Reference xqwen35.h:77: kept for link compatibility. The Vulkan path is not part of this
+ * library; like the reference on a host without Vulkan it writes a JSON saying so and
+ * returns XQ_ERR_RUNTIME (vulkan_backend.cpp:1638-1656). */
+XQ_API xq_status xq_run_vulkan_w4a16_selftest(char* json_out, size_t json_capacity);
+
+/* ---- CUDA extension (no reference counterpart) ------------------------------------ */
+typedef struct xq_cuda_options {
+    size_t struct_size;
+    int device;        /* CUDA device ordinal; -1 = XQ_CUDA_DEVICE env var or 0 */
+    int kv_fp16;       /* 1 = fp16 KV cache, 0 = fp32 KV cache (the reference's precision) */
+    int use_graphs;    /* 1 = capture each decode / prefill step as a CUDA graph (default) */
+} xq_cuda_options;
+
+/* xq_create with an explicit device and KV precision; xq_create uses the defaults
+ * (device from XQ_CUDA_DEVICE or 0, fp32 KV unless XQ_KV_FP16=1, graphs on). */
+XQ_API xq_status xq_create_cuda(const char* model_dir,
+                                const xq_options* options,
+                                const xq_cuda_options* cuda_options,
+                                xq_session** out_session);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XQWEN35_H_ */

@@ -1,0 +1,744 @@
+// DeviceModel: loads a reference-format package onto one B200, keeps weights, KV cache and
+// recurrent state resident, and runs each token step as one CUDA graph whose kernels are
+// chained with programmatic dependent launch.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <fstream>
+#include <sstream>
+
+#include "model.hpp"
+#include "ops.cuh"
+
+namespace xqb {
+
+namespace {
+
+std::string read_small_file(const std::string& path) {
+    std::ifstream in(path, std::ios::binary);
+    if (!in) return {};
+    std::ostringstream oss;
+    oss << in.rdbuf();
+    return oss.str();
+}
+
+bool file_exists(const std::string& path) {
+    std::ifstream in(path, std::ios::binary);
+    return in.good();
+}
+
+// findJsonInt / findJsonFloat (custom_model.cpp:38-87): first occurrence of "key", then the
+// first character of "-0123456789" after the next ':'.
+size_t json_value_pos(const std::string& json, const std::string& key) {
+    const std::string needle = "\"" + key + "\"";
+    const size_t pos = json.find(needle);
+    if (pos == std::string::npos) return std::string::npos;
+    const size_t colon = json.find(':', pos + needle.size());
+    if (colon == std::string::npos) return std::string::npos;
+    return json.find_first_of("-0123456789", colon + 1);
+}
+
+int json_int(const std::string& json, const std::string& key, int fallback) {
+    const size_t first = json_value_pos(json, key);
+    if (first == std::string::npos) return fallback;
+    size_t last = first + 1;
+    while (last < json.size() && json[last] >= '0' && json[last] <= '9') ++last;
+    try {
+        return std::stoi(json.substr(first, last - first));
+    } catch (...) {
+        return fallback;
+    }
+}
+
+float json_float(const std::string& json, const std::string& key, float fallback) {
+    const size_t first = json_value_pos(json, key);
+    if (first == std::string::npos) return fallback;
+    size_t last = first + 1;
+    while (last < json.size() && (std::isdigit(static_cast<unsigned char>(json[last])) || json[last] == '.' ||
+                                  json[last] == 'e' || json[last] == 'E' || json[last] == '-' || json[last] == '+'))
+        ++last;
+    try {
+        return std::stof(json.substr(first, last - first));
+    } catch (...) {
+        return fallback;
+    }
+}
+
+bool read_vec(const std::string& path, int expected, std::vector<float>* out, std::string* error) {
+    std::ifstream in(path, std::ios::binary);
+    if (!in) {
+        *error = "missing vector file: " + path;
+        return false;
+    }
+    out->assign(static_cast<size_t>(expected), 0.0f);
+    in.read(reinterpret_cast<char*>(out->data()), static_cast<std::streamsize>(out->size() * 4));
+    if (in.gcount() != static_cast<std::streamsize>(out->size() * 4)) {
+        *error = "short vector file: " + path;
+        return false;
+    }
+    return true;
+}
+
+void add_one(std::vector<float>* v) {
+    for (float& x : *v) x += 1.0f;
+}
+
+std::string shape_str(const HostMatrix& m) { return std::to_string(m.rows) + "x" + std::to_string(m.cols); }
+
+bool expect_shape(const HostMatrix& m, int rows, int cols, const std::string& name, std::string* error) {
+    if (m.rows != rows || m.cols != cols) {
+        *error = "unexpected shape for " + name + ": " + shape_str(m) + ", expected " + std::to_string(rows) + "x" +
+                 std::to_string(cols);
+        return false;
+    }
+    return true;
+}
+
+}  // namespace
+
+ModelDims parse_manifest(const std::string& js, int* n_layers) {
+    ModelDims d;  // defaults: custom_model.hpp:98-114
+    d.hidden = json_int(js, "hidden_size", d.hidden);
+    d.inter = json_int(js, "intermediate_size", d.inter);
+    d.vocab = json_int(js, "vocab_size", d.vocab);
+    d.heads = json_int(js, "num_attention_heads", d.heads);
+    d.kv_heads = json_int(js, "num_key_value_heads", d.kv_heads);
+    d.head_dim = json_int(js, "head_dim", d.head_dim);
+    const float partial = json_float(js, "partial_rotary_factor", 0.25f);
+    d.rotary_dim = std::max(2, static_cast<int>(std::round(static_cast<float>(d.head_dim) * partial)));
+    if (d.rotary_dim & 1) --d.rotary_dim;  // custom_model.cpp:438-442
+    d.lk_hd = json_int(js, "linear_key_head_dim", d.lk_hd);
+    d.lv_hd = json_int(js, "linear_value_head_dim", d.lv_hd);
+    d.lk_heads = json_int(js, "linear_num_key_heads", d.lk_heads);
+    d.lv_heads = json_int(js, "linear_num_value_heads", d.lv_heads);
+    d.conv_k = json_int(js, "linear_conv_kernel_dim", d.conv_k);
+    d.lk_dim = d.lk_hd * d.lk_heads;
+    d.lv_dim = d.lv_hd * d.lv_heads;
+    d.conv_dim = 2 * d.lk_dim + d.lv_dim;
+    d.eps = json_float(js, "rms_norm_eps", d.eps);
+    d.theta = json_float(js, "rope_theta", d.theta);
+    d.layers = json_int(js, "num_hidden_layers", 32);
+    if (n_layers) *n_layers = d.layers;
+    return d;
+}
+
+DeviceModel::~DeviceModel() {
+    if (!stream_ && allocs_.empty()) return;
+    cudaSetDevice(opts_.device);
+    if (stream_) cudaStreamSynchronize(stream_);
+    destroy_graphs();
+    for (DevLayer& L : layers_) {
+        free_matrix(&L.in_proj);
+        free_matrix(&L.out_proj);
+        free_matrix(&L.gate_up);
+        free_matrix(&L.down);
+        cudaFree(L.k_cache);
+        cudaFree(L.v_cache);
+    }
+    free_matrix(&lm_head_);
+    for (void* p : allocs_) cudaFree(p);
+    if (h_token_) cudaFreeHost(h_token_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+template <typename T>
+bool DeviceModel::dev_alloc(T** p, size_t count, std::string* error) {
+    *p = nullptr;
+    const size_t bytes = std::max<size_t>(1, count) * sizeof(T);
+    const cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), bytes);
+    if (e != cudaSuccess) {
+        *error = std::string("device allocation failed: ") + cudaGetErrorString(e);
+        return false;
+    }
+    allocs_.push_back(*p);
+    device_bytes_ += bytes;
+    if (cudaMemset(*p, 0, bytes) != cudaSuccess) {
+        *error = "cudaMemset failed";
+        return false;
+    }
+    return true;
+}
+
+bool DeviceModel::upload_vec(float** dst, const std::vector<float>& v, std::string* error) {
+    if (!dev_alloc(dst, v.size(), error)) return false;
+    if (cudaMemcpy(*dst, v.data(), v.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+        *error = "vector upload failed";
+        return false;
+    }
+    return true;
+}
+
+bool DeviceModel::load(const std::string& dir, const Options& opts, std::string* error) {
+    opts_ = opts;
+    if (cudaSetDevice(opts.device) != cudaSuccess) {
+        *error = "CUDA device " + std::to_string(opts.device) + " unavailable";
+        return false;
+    }
+    cudaDeviceGetAttribute(&num_sms_, cudaDevAttrMultiProcessorCount, opts.device);
+    if (cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking) != cudaSuccess) {
+        *error = "cudaStreamCreate failed";
+        return false;
+    }
+    if (!gemv_init_device()) {
+        *error = last_error();
+        return false;
+    }
+    if (attention_init_device(200 * 1024) != cudaSuccess) {
+        *error = "attention kernel setup failed";
+        return false;
+    }
+
+    int n_layers = 0;
+    d_ = parse_manifest(read_small_file(dir + "/xqwen35_manifest.json"), &n_layers);
+    const ModelDims& d = d_;
+    // Shapes the fused kernels are written for (all Qwen3.5-9B shapes satisfy them).
+    if (d.head_dim != 256 || d.rotary_dim != 64 || d.lk_hd != 128 || d.lv_hd % 32 != 0 || d.lv_hd > 1024 ||
+        (d.lv_hd & (d.lv_hd - 1)) != 0 || d.kv_heads <= 0 || d.heads % d.kv_heads != 0 ||
+        d.heads / d.kv_heads > kAttnMaxGroup || d.lk_heads <= 0 || d.lv_heads % d.lk_heads != 0 ||
+        d.conv_k < 1 || !fast_shape(d.hidden, 64) || !fast_shape(d.inter, 64) || !fast_shape(d.lv_dim, 64) ||
+        !fast_shape(d.heads * d.head_dim, 64) || n_layers <= 0) {
+        *error = "model shape not supported by the CUDA path (needs head_dim 256, rotary 64, linear key head 128, "
+                 "widths multiple of 1024, group 64)";
+        return false;
+    }
+    if (!file_exists(dir + "/embeddings_bf16.bin")) {
+        *error = "missing embeddings_bf16.bin";
+        return false;
+    }
+    std::vector<float> v;
+    if (!read_vec(dir + "/norm_weight.f32", d.hidden, &v, error)) return false;
+    add_one(&v);
+    if (!upload_vec(&d_final_norm_, v, error)) return false;
+    {
+        HostMatrix lm;
+        if (!read_xq4_file(dir + "/lm_head_weight.xq4", &lm, error)) return false;
+        if (!expect_shape(lm, d.vocab, d.hidden, "lm_head", error)) return false;
+        if (lm.group != 64) {
+            *error = "group size " + std::to_string(lm.group) + " not supported by the CUDA path";
+            return false;
+        }
+        if (!upload_matrix({&lm}, false, &lm_head_, error)) return false;
+        weight_bytes_ += lm_head_.bytes;
+    }
+    layers_.resize(static_cast<size_t>(n_layers));
+    for (int i = 0; i < n_layers; ++i) {
+        DevLayer& L = layers_[static_cast<size_t>(i)];
+        const std::string p = dir + "/layers_" + std::to_string(i) + "_";
+        HostMatrix gate, up, down;
+        if (!read_vec(p + "input_layernorm_weight.f32", d.hidden, &v, error)) return false;
+        add_one(&v);
+        if (!upload_vec(&L.input_norm, v, error)) return false;
+        if (!read_vec(p + "post_attention_layernorm_weight.f32", d.hidden, &v, error)) return false;
+        add_one(&v);
+        if (!upload_vec(&L.post_norm, v, error)) return false;
+        if (!read_xq4_file(p + "mlp_gate_proj_weight.xq4", &gate, error) ||
+            !read_xq4_file(p + "mlp_up_proj_weight.xq4", &up, error) ||
+            !read_xq4_file(p + "mlp_down_proj_weight.xq4", &down, error))
+            return false;
+        if (!expect_shape(gate, d.inter, d.hidden, "mlp_gate_proj", error) ||
+            !expect_shape(up, d.inter, d.hidden, "mlp_up_proj", error) ||
+            !expect_shape(down, d.hidden, d.inter, "mlp_down_proj", error))
+            return false;
+        if (!upload_matrix({&gate, &up}, true, &L.gate_up, error) || !upload_matrix({&down}, false, &L.down, error))
+            return false;
+        // custom_model.cpp:526: full attention iff the q_proj file exists.
+        L.full = file_exists(p + "self_attn_q_proj_weight.xq4");
+        if (L.full) {
+            HostMatrix q, k, vv, o;
+            if (!read_xq4_file(p + "self_attn_q_proj_weight.xq4", &q, error) ||
+                !read_xq4_file(p + "self_attn_k_proj_weight.xq4", &k, error) ||
+                !read_xq4_file(p + "self_attn_v_proj_weight.xq4", &vv, error) ||
+                !read_xq4_file(p + "self_attn_o_proj_weight.xq4", &o, error))
+                return false;
+            const int qd = d.heads * d.head_dim, kvd = d.kv_heads * d.head_dim;
+            if (!expect_shape(q, 2 * qd, d.hidden, "self_attn_q_proj (gated)", error) ||
+                !expect_shape(k, kvd, d.hidden, "self_attn_k_proj", error) ||
+                !expect_shape(vv, kvd, d.hidden, "self_attn_v_proj", error) ||
+                !expect_shape(o, d.hidden, qd, "self_attn_o_proj", error))
+                return false;
+            if (!upload_matrix({&q, &k, &vv}, false, &L.in_proj, error) ||
+                !upload_matrix({&o}, false, &L.out_proj, error))
+                return false;
+            if (!read_vec(p + "self_attn_q_norm_weight.f32", d.head_dim, &v, error)) return false;
+            add_one(&v);
+            if (!upload_vec(&L.q_norm, v, error)) return false;
+            if (!read_vec(p + "self_attn_k_norm_weight.f32", d.head_dim, &v, error)) return false;
+            add_one(&v);
+            if (!upload_vec(&L.k_norm, v, error)) return false;
+        } else {
+            HostMatrix qkv, a, b, z, o;
+            if (!read_xq4_file(p + "linear_attn_in_proj_qkv_weight.xq4", &qkv, error) ||
+                !read_xq4_file(p + "linear_attn_in_proj_a_weight.xq4", &a, error) ||
+                !read_xq4_file(p + "linear_attn_in_proj_b_weight.xq4", &b, error) ||
+                !read_xq4_file(p + "linear_attn_in_proj_z_weight.xq4", &z, error) ||
+                !read_xq4_file(p + "linear_attn_out_proj_weight.xq4", &o, error))
+                return false;
+            if (!expect_shape(qkv, d.conv_dim, d.hidden, "linear_attn_in_proj_qkv", error) ||
+                !expect_shape(a, d.lv_heads, d.hidden, "linear_attn_in_proj_a", error) ||
+                !expect_shape(b, d.lv_heads, d.hidden, "linear_attn_in_proj_b", error) ||
+                !expect_shape(z, d.lv_dim, d.hidden, "linear_attn_in_proj_z", error) ||
+                !expect_shape(o, d.hidden, d.lv_dim, "linear_attn_out_proj", error))
+                return false;
+            if (!upload_matrix({&qkv, &z, &a, &b}, false, &L.in_proj, error) ||
+                !upload_matrix({&o}, false, &L.out_proj, error))
+                return false;
+            if (!read_vec(p + "linear_attn_norm_weight.f32", d.lv_hd, &v, error)) return false;
+            if (!upload_vec(&L.lin_norm, v, error)) return false;
+            if (!read_vec(p + "linear_attn_conv1d_weight.f32", d.conv_dim * d.conv_k, &v, error)) return false;
+            if (!upload_vec(&L.conv_w, v, error)) return false;
+            if (!read_vec(p + "linear_attn_A_log.f32", d.lv_heads, &v, error)) return false;
+            if (!upload_vec(&L.a_log, v, error)) return false;
+            if (!read_vec(p + "linear_attn_dt_bias.f32", d.lv_heads, &v, error)) return false;
+            if (!upload_vec(&L.dt_bias, v, error)) return false;
+            if (!dev_alloc(&L.conv_state, static_cast<size_t>(d.conv_dim) * std::max(0, d.conv_k - 1), error) ||
+                !dev_alloc(&L.rec_state, static_cast<size_t>(d.lv_heads) * d.lk_hd * d.lv_hd, error))
+                return false;
+        }
+        for (const DevMatrix* m : {&L.in_proj, &L.out_proj, &L.gate_up, &L.down}) {
+            if (!m->fast()) {
+                *error = "layer " + std::to_string(i) + ": matrix shape not supported by the fused kernels";
+                return false;
+            }
+            weight_bytes_ += m->bytes;
+        }
+    }
+    if (!lm_head_.fast()) {
+        *error = "lm_head shape not supported by the fused kernels";
+        return false;
+    }
+    // Embedding table, resident in device memory (the reference reads one row from disk
+    // per token, custom_model.cpp:569-608).
+    {
+        const size_t bytes = static_cast<size_t>(d.vocab) * d.hidden * 2;
+        std::ifstream in(dir + "/embeddings_bf16.bin", std::ios::binary);
+        if (!dev_alloc(&d_emb_, bytes / 2, error)) return false;
+        const size_t chunk = 64u << 20;
+        void* staging = nullptr;
+        if (cudaMallocHost(&staging, chunk) != cudaSuccess) {
+            *error = "pinned staging allocation failed";
+            return false;
+        }
+        size_t done = 0;
+        bool ok = true;
+        while (done < bytes && ok) {
+            const size_t n = std::min(chunk, bytes - done);
+            in.read(static_cast<char*>(staging), static_cast<std::streamsize>(n));
+            if (in.gcount() != static_cast<std::streamsize>(n)) {
+                ok = false;
+                break;
+            }
+            ok = cudaMemcpy(reinterpret_cast<uint8_t*>(d_emb_) + done, staging, n, cudaMemcpyHostToDevice) ==
+                 cudaSuccess;
+            done += n;
+        }
+        cudaFreeHost(staging);
+        if (!ok) {
+            *error = "short embeddings_bf16.bin";
+            return false;
+        }
+    }
+    const int qkv_rows = 2 * d.heads * d.head_dim + 2 * d.kv_heads * d.head_dim;
+    const int group = d.heads / d.kv_heads;
+    if (!dev_alloc(&d_hidden_, d.hidden, error) || !dev_alloc(&d_conv_out_, d.conv_dim, error) ||
+        !dev_alloc(&d_zab_, d.lv_dim + 2 * d.lv_heads, error) || !dev_alloc(&d_attn_raw_, d.lv_dim, error) ||
+        !dev_alloc(&d_qkv_, qkv_rows, error) || !dev_alloc(&d_attn_out_, d.heads * d.head_dim, error) ||
+        !dev_alloc(&d_ffn_, d.inter, error) || !dev_alloc(&d_normed_, d.hidden, error) ||
+        !dev_alloc(&d_logits_, d.vocab, error) || !dev_alloc(&d_pos_, 1, error) || !dev_alloc(&d_next_pos_, 1, error) ||
+        !dev_alloc(&d_token_, 1, error) || !dev_alloc(&d_ring_, ring_cap_, error) ||
+        !dev_alloc(&d_ring_ctr_, 1, error) || !dev_alloc(&d_arg_val_, num_sms_, error) ||
+        !dev_alloc(&d_arg_idx_, num_sms_, error) || !dev_alloc(&d_arg_counter_, 1, error) ||
+        !dev_alloc(&d_attn_part_, static_cast<size_t>(d.kv_heads) * kAttnSplits * group * (d.head_dim + 2), error) ||
+        !dev_alloc(&d_attn_counters_, d.kv_heads, error) || !dev_alloc(&d_err_, 1, error))
+        return false;
+    if (cudaMallocHost(&h_token_, sizeof(int32_t)) != cudaSuccess) {
+        *error = "pinned allocation failed";
+        return false;
+    }
+    if (!alloc_kv(std::max(64, opts.initial_capacity), error)) return false;
+    if (cudaDeviceSynchronize() != cudaSuccess) {
+        *error = "device synchronisation after load failed";
+        return false;
+    }
+    loaded_ = true;
+    return true;
+}
+
+bool DeviceModel::alloc_kv(int capacity, std::string* error) {
+    const size_t elem = opts_.kv_fp16 ? 2 : 4;
+    const size_t per_pos = static_cast<size_t>(d_.kv_heads) * d_.head_dim * elem;
+    for (DevLayer& L : layers_) {
+        if (!L.full) continue;
+        void *k = nullptr, *v = nullptr;
+        if (cudaMalloc(&k, per_pos * capacity) != cudaSuccess || cudaMalloc(&v, per_pos * capacity) != cudaSuccess) {
+            cudaFree(k);
+            *error = "KV cache allocation failed for capacity " + std::to_string(capacity);
+            return false;
+        }
+        cudaMemset(k, 0, per_pos * capacity);
+        cudaMemset(v, 0, per_pos * capacity);
+        if (L.k_cache) {  // keep positions already written
+            const size_t keep = per_pos * std::min(capacity_, capacity);
+            cudaMemcpyAsync(k, L.k_cache, keep, cudaMemcpyDeviceToDevice, stream_);
+            cudaMemcpyAsync(v, L.v_cache, keep, cudaMemcpyDeviceToDevice, stream_);
+            cudaStreamSynchronize(stream_);
+            cudaFree(L.k_cache);
+            cudaFree(L.v_cache);
+            device_bytes_ -= 2 * per_pos * capacity_;
+        }
+        L.k_cache = k;
+        L.v_cache = v;
+        device_bytes_ += 2 * per_pos * capacity;
+    }
+    capacity_ = capacity;
+    return true;
+}
+
+bool DeviceModel::ensure_capacity(int needed, std::string* error) {
+    if (needed <= capacity_) return true;
+    int cap = capacity_;
+    while (cap < needed) cap *= 2;
+    if (attention_smem_bytes(d_.heads, d_.kv_heads, d_.head_dim, cap) > 200 * 1024) {
+        *error = "context length " + std::to_string(needed) + " exceeds the attention kernel's limit";
+        return false;
+    }
+    destroy_graphs();  // graphs hold the old cache pointers and the attention smem size
+    return alloc_kv(cap, error);
+}
+
+int DeviceModel::kernels_per_decode_step() const {
+    int n = 1;  // lm_head argmax + embedding
+    for (const DevLayer& L : layers_) n += L.full ? 5 : 5;
+    return n;
+}
+
+int DeviceModel::kernels_per_prefill_step() const { return kernels_per_decode_step(); }
+
+bool DeviceModel::enqueue_forward(cudaStream_t s) {
+    const ModelDims& d = d_;
+    LaunchCtx ctx;
+    ctx.stream = s;
+    ctx.num_sms = num_sms_;
+    ctx.pdl = true;
+    for (DevLayer& L : layers_) {
+        if (!L.full) {
+            GemvParams p = {};
+            p.x = d_hidden_;
+            p.norm_w = L.input_norm;
+            p.eps = d.eps;
+            p.out = d_conv_out_;
+            p.out2 = d_zab_;
+            p.conv_w = L.conv_w;
+            p.conv_state = L.conv_state;
+            p.conv_channels = d.conv_dim;
+            p.conv_k = d.conv_k;
+            p.err = d_err_;
+            if (!launch_gemv(L.in_proj, kProRms, kEpiConv, p, 1, ctx)) return false;
+            DeltaParams dp{d_conv_out_, d_zab_ + d.lv_dim, L.a_log, L.dt_bias, L.rec_state, d_attn_raw_,
+                           d.lk_heads, d.lv_heads, d.lk_hd, d.lv_hd};
+            if (launch_ex(gated_delta_kernel, dim3(d.lv_heads, d.lv_hd / kDeltaCols), dim3(d.lk_hd), 0, s, true,
+                          dp) != cudaSuccess) {
+                set_last_error("gated delta launch failed");
+                return false;
+            }
+            GemvParams q = {};
+            q.x = d_attn_raw_;
+            q.norm_w = L.lin_norm;
+            q.gate_z = d_zab_;
+            q.head_dim = d.lv_hd;
+            q.eps = d.eps;
+            q.out = d_hidden_;
+            q.err = d_err_;
+            if (!launch_gemv(L.out_proj, kProGatedRms, kEpiResidual, q, 1, ctx)) return false;
+        } else {
+            GemvParams p = {};
+            p.x = d_hidden_;
+            p.norm_w = L.input_norm;
+            p.eps = d.eps;
+            p.out = d_qkv_;
+            p.err = d_err_;
+            if (!launch_gemv(L.in_proj, kProRms, kEpiStore, p, 1, ctx)) return false;
+            AttnParams ap = {};
+            ap.qkv = d_qkv_;
+            ap.q_norm = L.q_norm;
+            ap.k_norm = L.k_norm;
+            ap.k_cache = L.k_cache;
+            ap.v_cache = L.v_cache;
+            ap.capacity = capacity_;
+            ap.pos_ptr = d_pos_;
+            ap.nq = d.heads;
+            ap.nkv = d.kv_heads;
+            ap.hd = d.head_dim;
+            ap.rotary = d.rotary_dim;
+            ap.theta = d.theta;
+            ap.eps = d.eps;
+            ap.part = d_attn_part_;
+            ap.counters = d_attn_counters_;
+            ap.out = d_attn_out_;
+            ap.err = d_err_;
+            const size_t smem = attention_smem_bytes(d.heads, d.kv_heads, d.head_dim, capacity_);
+            const cudaError_t e = launch_attention(ap, opts_.kv_fp16, smem, s, true);
+            if (e != cudaSuccess) {
+                set_last_error(std::string("attention launch failed: ") + cudaGetErrorString(e));
+                return false;
+            }
+            GemvParams q = {};
+            q.x = d_attn_out_;
+            q.out = d_hidden_;
+            q.err = d_err_;
+            if (!launch_gemv(L.out_proj, kProPlain, kEpiResidual, q, 1, ctx)) return false;
+        }
+        GemvParams g = {};
+        g.x = d_hidden_;
+        g.norm_w = L.post_norm;
+        g.eps = d.eps;
+        g.out = d_ffn_;
+        g.err = d_err_;
+        if (!launch_gemv(L.gate_up, kProRms, kEpiSwiglu, g, 2, ctx)) return false;
+        GemvParams dn = {};
+        dn.x = d_ffn_;
+        dn.out = d_hidden_;
+        dn.err = d_err_;
+        if (!launch_gemv(L.down, kProPlain, kEpiResidual, dn, 1, ctx)) return false;
+    }
+    return true;
+}
+
+bool DeviceModel::enqueue_decode_step(cudaStream_t s) {
+    LaunchCtx ctx;
+    ctx.stream = s;
+    ctx.num_sms = num_sms_;
+    ctx.pdl = true;
+    GemvParams p = {};
+    p.x = d_hidden_;
+    p.norm_w = d_final_norm_;  // runFinalNorm, custom_model.cpp:1258-1279
+    p.eps = d_.eps;
+    p.part_val = d_arg_val_;
+    p.part_idx = d_arg_idx_;
+    p.counter = d_arg_counter_;
+    p.token_out = d_token_;
+    p.emb = d_emb_;
+    p.hidden_out = d_hidden_;
+    p.hidden = d_.hidden;
+    p.pos = d_pos_;
+    p.next_pos = d_next_pos_;
+    p.ring = d_ring_;
+    p.ring_ctr = d_ring_ctr_;
+    p.ring_cap = ring_cap_;
+    p.err = d_err_;
+    if (!launch_gemv(lm_head_, kProRms, kEpiArgmax, p, 1, ctx, num_sms_)) return false;
+    return enqueue_forward(s);
+}
+
+bool DeviceModel::enqueue_prefill_step(cudaStream_t s) {
+    if (launch_ex(embed_prefill_kernel, dim3(1), dim3(512), 0, s, true, static_cast<const int*>(d_prompt_),
+                  static_cast<const uint16_t*>(d_emb_), d_hidden_, d_.hidden, d_.vocab, d_pos_, d_next_pos_) !=
+        cudaSuccess) {
+        set_last_error("embedding launch failed");
+        return false;
+    }
+    return enqueue_forward(s);
+}
+
+void DeviceModel::destroy_graphs() {
+    if (g_decode_) cudaGraphExecDestroy(g_decode_);
+    if (g_prefill_) cudaGraphExecDestroy(g_prefill_);
+    g_decode_ = g_prefill_ = nullptr;
+}
+
+bool DeviceModel::capture_graphs(std::string* error) {
+    for (int which = 0; which < 2; ++which) {
+        cudaGraph_t graph = nullptr;
+        if (cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+            *error = "cudaStreamBeginCapture failed";
+            return false;
+        }
+        const bool ok = which == 0 ? enqueue_decode_step(stream_) : enqueue_prefill_step(stream_);
+        const cudaError_t e = cudaStreamEndCapture(stream_, &graph);
+        if (!ok || e != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            *error = std::string("graph capture failed: ") + (ok ? cudaGetErrorString(e) : last_error());
+            return false;
+        }
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ie != cudaSuccess) {
+            *error = std::string("graph instantiate failed: ") + cudaGetErrorString(ie);
+            return false;
+        }
+        (which == 0 ? g_decode_ : g_prefill_) = exec;
+    }
+    return true;
+}
+
+bool DeviceModel::run_step(bool decode, std::string* error) {
+    if (!ensure_capacity(position_ + 1, error)) return false;
+    if (opts_.use_graphs) {
+        if (!g_decode_ && !capture_graphs(error)) return false;
+        const cudaError_t e = cudaGraphLaunch(decode ? g_decode_ : g_prefill_, stream_);
+        if (e != cudaSuccess) {
+            *error = std::string("graph launch failed: ") + cudaGetErrorString(e);
+            return false;
+        }
+    } else {
+        if (!(decode ? enqueue_decode_step(stream_) : enqueue_prefill_step(stream_))) {
+            *error = last_error();
+            return false;
+        }
+    }
+    ++position_;
+    if (decode) ++ring_count_;
+    return true;
+}
+
+bool DeviceModel::reset(std::string* error) {
+    if (!loaded_) {
+        *error = "model not loaded";
+        return false;
+    }
+    for (DevLayer& L : layers_) {
+        if (L.full) continue;
+        cudaMemsetAsync(L.conv_state, 0, sizeof(float) * d_.conv_dim * std::max(0, d_.conv_k - 1), stream_);
+        cudaMemsetAsync(L.rec_state, 0, sizeof(float) * d_.lv_heads * d_.lk_hd * d_.lv_hd, stream_);
+    }
+    cudaMemsetAsync(d_pos_, 0, sizeof(int), stream_);
+    cudaMemsetAsync(d_next_pos_, 0, sizeof(int), stream_);
+    cudaMemsetAsync(d_ring_ctr_, 0, sizeof(int), stream_);
+    position_ = 0;
+    ring_count_ = 0;
+    if (cudaStreamSynchronize(stream_) != cudaSuccess) {
+        *error = std::string("reset failed: ") + cudaGetErrorString(cudaGetLastError());
+        return false;
+    }
+    return true;
+}
+
+bool DeviceModel::prefill(const int32_t* ids, size_t n, std::string* error) {
+    if (!ids || n == 0) {
+        *error = "custom prefill requires prompt tokens";
+        return false;
+    }
+    cudaSetDevice(opts_.device);
+    if (!reset(error)) return false;
+    if (n > prompt_cap_) {
+        if (d_prompt_) cudaFree(d_prompt_);
+        d_prompt_ = nullptr;
+        prompt_cap_ = 0;
+        if (cudaMalloc(&d_prompt_, n * sizeof(int)) != cudaSuccess) {
+            *error = "prompt allocation failed";
+            return false;
+        }
+        prompt_cap_ = n;
+        destroy_graphs();  // the prefill graph holds the prompt pointer
+    }
+    if (cudaMemcpyAsync(d_prompt_, ids, n * sizeof(int), cudaMemcpyHostToDevice, stream_) != cudaSuccess) {
+        *error = "prompt upload failed";
+        return false;
+    }
+    for (size_t i = 0; i < n; ++i)
+        if (!run_step(false, error)) return false;
+    const cudaError_t e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess) {
+        *error = std::string("prefill failed: ") + cudaGetErrorString(e);
+        return false;
+    }
+    if (device_errors()) {
+        *error = "device wait budget exceeded during prefill";
+        return false;
+    }
+    return true;
+}
+
+bool DeviceModel::decode_one(int32_t* token, std::string* error) {
+    cudaSetDevice(opts_.device);
+    if (!run_step(true, error)) return false;
+    if (cudaMemcpyAsync(h_token_, d_token_, sizeof(int32_t), cudaMemcpyDeviceToHost, stream_) != cudaSuccess) {
+        *error = "token copy failed";
+        return false;
+    }
+    const cudaError_t e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess) {
+        *error = std::string("decode failed: ") + cudaGetErrorString(e);
+        return false;
+    }
+    *token = *h_token_;
+    return true;
+}
+
+bool DeviceModel::decode_many(size_t count, std::string* error) {
+    cudaSetDevice(opts_.device);
+    for (size_t i = 0; i < count; ++i)
+        if (!run_step(true, error)) return false;
+    return true;
+}
+
+bool DeviceModel::read_ring(size_t first, size_t count, int32_t* out, std::string* error) {
+    if (count > static_cast<size_t>(ring_cap_)) {
+        *error = "too many tokens requested from the device ring";
+        return false;
+    }
+    for (size_t i = 0; i < count;) {
+        const size_t idx = (first + i) % ring_cap_;
+        const size_t n = std::min(count - i, ring_cap_ - idx);
+        if (cudaMemcpyAsync(out + i, d_ring_ + idx, n * sizeof(int32_t), cudaMemcpyDeviceToHost, stream_) !=
+            cudaSuccess) {
+            *error = "token ring copy failed";
+            return false;
+        }
+        i += n;
+    }
+    const cudaError_t e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess) {
+        *error = std::string("decode failed: ") + cudaGetErrorString(e);
+        return false;
+    }
+    return true;
+}
+
+bool DeviceModel::hidden(std::vector<float>* out, std::string* error) {
+    cudaSetDevice(opts_.device);
+    rmsnorm_kernel<<<1, 1024, 0, stream_>>>(d_hidden_, d_final_norm_, d_.hidden, d_.eps, d_normed_);
+    out->resize(static_cast<size_t>(d_.hidden));
+    cudaMemcpyAsync(out->data(), d_normed_, out->size() * 4, cudaMemcpyDeviceToHost, stream_);
+    const cudaError_t e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess) {
+        *error = std::string("hidden state copy failed: ") + cudaGetErrorString(e);
+        return false;
+    }
+    return true;
+}
+
+bool DeviceModel::logits(std::vector<float>* out, std::string* error) {
+    cudaSetDevice(opts_.device);
+    rmsnorm_kernel<<<1, 1024, 0, stream_>>>(d_hidden_, d_final_norm_, d_.hidden, d_.eps, d_normed_);
+    GemvParams p = {};
+    p.x = d_normed_;
+    p.out = d_logits_;
+    p.err = d_err_;
+    LaunchCtx ctx;
+    ctx.stream = stream_;
+    ctx.num_sms = num_sms_;
+    ctx.pdl = false;
+    if (!launch_gemv(lm_head_, kProPlain, kEpiStore, p, 1, ctx)) {
+        *error = last_error();
+        return false;
+    }
+    out->resize(static_cast<size_t>(d_.vocab));
+    cudaMemcpyAsync(out->data(), d_logits_, out->size() * 4, cudaMemcpyDeviceToHost, stream_);
+    const cudaError_t e = cudaStreamSynchronize(stream_);
+    if (e != cudaSuccess) {
+        *error = std::string("logits failed: ") + cudaGetErrorString(e);
+        return false;
+    }
+    return true;
+}
+
+unsigned DeviceModel::device_errors() {
+    unsigned v = 0;
+    cudaMemcpy(&v, d_err_, sizeof v, cudaMemcpyDeviceToHost);
+    return v;
+}
+
+}  // namespace xqb

@@ -1,0 +1,141 @@
+// Device-resident model for the decode hot path (replaces the reference's CustomModel,
+// customlib/runtime/custom_model.hpp:38-150, for the CUDA path).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "gemv.hpp"
+
+namespace xqb {
+
+struct ModelDims {
+    int hidden = 4096, inter = 12288, vocab = 248320;
+    int heads = 16, kv_heads = 4, head_dim = 256, rotary_dim = 64;
+    int lk_hd = 128, lv_hd = 128, lk_heads = 16, lv_heads = 32, conv_k = 4;
+    int lk_dim = 2048, lv_dim = 4096, conv_dim = 8192;
+    float eps = 1.0e-6f, theta = 10000000.0f;
+    int layers = 32;
+};
+
+// Manifest parsing with the reference's substring rules (custom_model.cpp:38-87, 431-453).
+ModelDims parse_manifest(const std::string& json, int* n_layers);
+
+struct DevLayer {
+    bool full = false;
+    DevMatrix in_proj;   // linear: [qkv | z | a | b]; full: [q(+gate) | k | v]
+    DevMatrix out_proj;  // linear: out_proj; full: o_proj
+    DevMatrix gate_up;   // rows interleaved gate_0, up_0, gate_1, ...
+    DevMatrix down;
+    float* input_norm = nullptr;  // +1 applied (custom_model.cpp:524)
+    float* post_norm = nullptr;
+    float* q_norm = nullptr;  // full, +1
+    float* k_norm = nullptr;
+    float* lin_norm = nullptr;  // linear, no +1 (custom_model.cpp:546)
+    float* conv_w = nullptr;
+    float* a_log = nullptr;
+    float* dt_bias = nullptr;
+    float* conv_state = nullptr;  // [conv_dim][conv_k - 1]
+    float* rec_state = nullptr;   // [lv_heads][lk_hd][lv_hd]
+    void* k_cache = nullptr;      // [capacity][kv_heads][head_dim]
+    void* v_cache = nullptr;
+};
+
+struct Options {
+    int device = 0;
+    bool kv_fp16 = false;
+    bool use_graphs = true;
+    int initial_capacity = 8192;
+};
+
+class DeviceModel {
+public:
+    DeviceModel() = default;
+    ~DeviceModel();
+    DeviceModel(const DeviceModel&) = delete;
+    DeviceModel& operator=(const DeviceModel&) = delete;
+
+    bool load(const std::string& model_dir, const Options& opts, std::string* error);
+    // CustomModel::resetState (custom_model.cpp:555-567) + position 0.
+    bool reset(std::string* error);
+    // CustomModel::prefill (custom_model.cpp:610-640): reset, then one forward per token.
+    bool prefill(const int32_t* ids, size_t n, std::string* error);
+    // CustomModel::decodeOne (custom_model.cpp:1340-1356): sample, then forward it.
+    bool decode_one(int32_t* token, std::string* error);
+    // Enqueue `count` decode steps without host synchronisation; tokens land in the ring.
+    bool decode_many(size_t count, std::string* error);
+    bool read_ring(size_t first, size_t count, int32_t* out, std::string* error);
+    // Post-final-norm hidden state (what copyHidden returns, custom_model.cpp:1438-1447).
+    bool hidden(std::vector<float>* out, std::string* error);
+    // Full lm_head logits of the current (normed) hidden state, for debug JSON.
+    bool logits(std::vector<float>* out, std::string* error);
+    // Device error word set by bounded waits; 0 when clean.
+    unsigned device_errors();
+
+    const ModelDims& dims() const { return d_; }
+    size_t weight_bytes() const { return weight_bytes_; }
+    size_t device_bytes() const { return device_bytes_; }
+    int position() const { return position_; }
+    int capacity() const { return capacity_; }
+    bool kv_fp16() const { return opts_.kv_fp16; }
+    int kernels_per_decode_step() const;
+    int kernels_per_prefill_step() const;
+    cudaStream_t stream() const { return stream_; }
+    const std::vector<DevLayer>& layers() const { return layers_; }
+    const DevMatrix& lm_head() const { return lm_head_; }
+    float* hidden_ptr() const { return d_hidden_; }
+    float* final_norm_ptr() const { return d_final_norm_; }
+    int num_sms() const { return num_sms_; }
+
+    // Launch sequences (used by graph capture and by the eager path).
+    bool enqueue_decode_step(cudaStream_t s);
+    bool enqueue_prefill_step(cudaStream_t s);
+
+private:
+    bool enqueue_forward(cudaStream_t s);
+    bool ensure_capacity(int needed, std::string* error);
+    bool alloc_kv(int capacity, std::string* error);
+    bool capture_graphs(std::string* error);
+    void destroy_graphs();
+    bool run_step(bool decode, std::string* error);
+    template <typename T>
+    bool dev_alloc(T** p, size_t count, std::string* error);
+    bool upload_vec(float** dst, const std::vector<float>& v, std::string* error);
+
+    ModelDims d_;
+    Options opts_;
+    std::vector<DevLayer> layers_;
+    DevMatrix lm_head_;
+    float* d_final_norm_ = nullptr;
+    uint16_t* d_emb_ = nullptr;
+    // activations
+    float *d_hidden_ = nullptr, *d_conv_out_ = nullptr, *d_zab_ = nullptr, *d_attn_raw_ = nullptr;
+    float *d_qkv_ = nullptr, *d_attn_out_ = nullptr, *d_ffn_ = nullptr, *d_normed_ = nullptr, *d_logits_ = nullptr;
+    // step control
+    int *d_pos_ = nullptr, *d_next_pos_ = nullptr, *d_token_ = nullptr, *d_ring_ = nullptr, *d_ring_ctr_ = nullptr;
+    int* d_prompt_ = nullptr;
+    size_t prompt_cap_ = 0;
+    float* d_arg_val_ = nullptr;
+    int* d_arg_idx_ = nullptr;
+    unsigned* d_arg_counter_ = nullptr;
+    float* d_attn_part_ = nullptr;
+    unsigned* d_attn_counters_ = nullptr;
+    unsigned* d_err_ = nullptr;
+    int32_t* h_token_ = nullptr;  // pinned
+    int ring_cap_ = 1 << 16;
+
+    cudaStream_t stream_ = nullptr;
+    cudaGraphExec_t g_decode_ = nullptr, g_prefill_ = nullptr;
+    int num_sms_ = 148;
+    int capacity_ = 0;
+    int position_ = 0;  // host mirror of *d_next_pos_
+    size_t ring_count_ = 0;  // host mirror of *d_ring_ctr_
+    size_t weight_bytes_ = 0, device_bytes_ = 0;
+    std::vector<void*> allocs_;
+    bool loaded_ = false;
+};
+
+}  // namespace xqb

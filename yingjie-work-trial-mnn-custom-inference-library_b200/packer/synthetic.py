@@ -121,7 +121,7 @@ def write_xq4(path: str, rows: int, cols: int, group: int, packed: np.ndarray, s
 
 def read_xq4(path: str) -> Dict:
     with open(path, "rb") as f:
-        head = f.read(48)
+        head = f.read(struct.calcsize("<8sIIIIIQQQ"))
         magic, version, rows, cols, group, bits, nbytes, nscale, nzero = struct.unpack("<8sIIIIIQQQ", head)
         if magic[:7] != XQ4_MAGIC[:7]:
             raise ValueError(f"bad xq4 magic: {path}")
