@@ -1,0 +1,306 @@
+"""Decode benchmark: Qwen3.5-9B-shaped W4A16 model, batch 1, on B200.
+
+Workload (config 2 of the benchmark definition): a seeded random-init 32-layer package
+(3:1 Gated-DeltaNet : full attention, vocab 248320, W4A16 g64, bf16 embeddings restricted
+to fp16-representable values), a 512-token prefill of uniform random ids, then greedy
+decode steps. A "step" is one decode token. `value` is decode tok/s over the timed steps
+with everything resident in HBM (device time from CUDA events on the session stream);
+`e2e` is the same metric through xq_decode_one (host call, token copied back every step).
+With --gpus N (torchrun) every rank runs an independent replica session on its own GPU
+(the path does not shard for replicas); value = all ranks' tokens / max rank time.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+import __graft_entry__  # noqa: E402
+
+PROMPT_LEN = 512
+SEED = 2024
+METRIC = "decode tok/s (9B W4A16, b=1)"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def package_dir():
+    base = os.environ.get("XQ_BENCH_DIR", os.path.join(os.environ.get("TMPDIR", "/tmp"), "xq_bench"))
+    return os.path.join(base, f"qwen35_9b_s{SEED}")
+
+
+def make_package(rank, world):
+    from xqwen35_b200.packer import synthetic
+
+    d = package_dir()
+    if rank == 0:
+        t = time.time()
+        synthetic.make_package(d, synthetic.preset("cfg2"), seed=SEED)
+        print(f"[bench] package ready in {time.time() - t:.1f}s: {d}", file=sys.stderr, flush=True)
+    return d
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm = [float(s[1]) for s in self.samples if len(s) >= 9 and s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if len(s) >= 9 and s[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            if len(s) >= 9:
+                for n, v in zip(names, s[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+def gemv_roofline(pkg, peak_gbs, iters=40):
+    """Time the dominant kernel, the fused W4A16 GEMV, at the largest per-layer shape of the
+    9B step (gate+up: 24576 x 4096) with CUDA events on the launching stream, rotating over
+    4 copies (214 MB, more than L2), and express it against the HBM roofline."""
+    import torch
+
+    rows, cols, ncopy = 24576, 4096, 4
+    mats = []
+    for i in range(ncopy):
+        rng = np.random.default_rng(100 + i)
+        packed = rng.integers(0, 256, rows * cols // 2, dtype=np.uint8)
+        s = (np.abs(rng.standard_normal(rows * cols // 64)) * 0.02).astype(np.float16).astype(np.float32)
+        mats.append(pkg.Matrix(packed, s, np.full(rows * cols // 64, 8.0, np.float32), rows, cols, 64))
+    x = torch.randn(cols, device="cuda")
+    y = torch.zeros(rows, device="cuda")
+    st = torch.cuda.current_stream()
+    for m in mats:
+        m.gemv(x.data_ptr(), y.data_ptr(), st.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(iters):
+        mats[i % ncopy].gemv(x.data_ptr(), y.data_ptr(), st.cuda_stream)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    alg = rows * cols // 2 + rows * (cols // 64) * 2 + 4 * cols + 4 * rows
+    achieved = alg / (ms * 1e-3) / 1e9
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "gemv_w4a16_gate_up_9b.md")
+    if os.path.exists(prof):
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.]+)", open(prof).read())
+        if m:
+            traffic = float(m.group(1))
+    for m in mats:
+        m.close()
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+            "frac": round(achieved / peak_gbs, 4), "traffic": traffic, "kernel": "gemv_w4a16_kernel",
+            "shape": f"{rows}x{cols}", "algorithmic_bytes": alg, "launch_us": round(ms * 1000, 2)}
+
+
+def cpu_baseline(model_dir, steps):
+    """The reference's own CPU path (compiled from its sources) on the same package, on a
+    bounded sample: an 8-token prompt then `steps` greedy decode tokens through its C ABI."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    cores = min(8, os.cpu_count() or 1)
+    ids = np.random.default_rng(SEED).integers(0, 248320, 8).astype(np.int32)
+    if oracle.ref_available():
+        s = oracle.RefSession(model_dir, threads=cores)
+        kind = "reference"
+    else:
+        oracle.port().xo_set_threads(cores)
+        s = oracle.PortModel(model_dir)
+        kind = "port"
+    s.prefill(ids)
+    t = time.time()
+    for _ in range(steps):
+        s.decode_one()
+    dt = time.time() - t
+    s.close()
+    return {"value": round(steps / dt, 4), "unit": "tok/s", "cores": cores, "kind": kind,
+            "sample": f"{steps} greedy decode steps after an 8-token prompt (context 8..{8 + steps}) on the 9B "
+                      f"package; the reference's WorkerPool caps at min(8, hardware_concurrency) threads"}
+
+
+def run_reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    d = make_package(0, 1)
+    steps = max(1, min(args.steps, 16))
+    warm = min(args.warmup, 1)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    if warm:
+        cpu_baseline(d, warm)
+    cb = cpu_baseline(d, steps)
+    line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
+            "steps": steps, "warmup": warm, "ms_per_step": round(1000.0 / cb["value"], 2) if cb["value"] else None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init package)",
+            "config": {"workload": "config2: Qwen3.5-9B-shaped W4A16 g64, 32 layers, vocab 248320, greedy decode",
+                       "prompt": 8, "kv_dtype": "f32", "cpu_sample": True},
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not oracle.ref_available():
+        line["cpu_baseline"]["kind"] = "port"
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--kv-fp16", action="store_true")
+    ap.add_argument("--cpu-steps", type=int, default=12)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=900))
+    pkg = __graft_entry__.load_package()
+    d = make_package(rank, world)
+    if world > 1:
+        dist.barrier()
+    sess = pkg.Session(d, device=local, kv_fp16=args.kv_fp16, max_context_tokens=PROMPT_LEN + args.warmup +
+                       args.steps + 128)
+    ids = np.random.default_rng(SEED + rank).integers(0, 248320, PROMPT_LEN).astype(np.int32)
+    m = sess.prefill(ids)
+    prefill_tok_s = m.prefill_tokens_per_second
+    sess.decode_timed(args.warmup)  # untimed warm-up steps (graph capture happens here)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        dev_ms, toks = sess.decode_timed(args.steps, want_tokens=True)
+        torch.cuda.synchronize()
+    t = torch.tensor([dev_ms], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.barrier()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # e2e: the same metric through xq_decode_one (host API call; 4-byte token read back per step)
+    e2e_steps = min(args.steps, 64)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        sess.decode_one()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * e2e_steps / float(te.item())
+
+    info = json.loads(sess.json("backend"))
+    kernels_per_step = int(info.get("kernels_per_decode_step", 0))
+    peak, peak_kind = peaks()
+    roof = gemv_roofline(pkg, peak) if rank == 0 else None
+    step_bytes = info.get("weight_bytes", 0)
+    if rank == 0:
+        ctx0 = PROMPT_LEN + args.warmup
+        kv_elem = 2 if args.kv_fp16 else 4
+        kv_bytes = 8 * 2 * 4 * 256 * kv_elem * (ctx0 + args.steps / 2)  # mean context over the timed steps
+        state_bytes = 24 * (2 * 32 * 128 * 128 * 4 + 2 * 8192 * 3 * 4)
+        alg_step = step_bytes + state_bytes + kv_bytes + 4096 * 2
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random-init 9B-shaped package)",
+            "config": {"workload": "config2: Qwen3.5-9B-shaped W4A16 g64 (32 layers, 3:1 DeltaNet:GQA, vocab "
+                                   "248320), 512-token random prompt, greedy decode, batch 1",
+                       "prompt": PROMPT_LEN, "context_during_timing": [PROMPT_LEN + args.warmup,
+                                                                        PROMPT_LEN + args.warmup + args.steps],
+                       "kv_dtype": "f16" if args.kv_fp16 else "f32", "parallelism": f"replicas{world}",
+                       "l2": "inputs larger than L2 (4.3 GB of weights streamed per step)",
+                       "cuda_graphs": True, "pdl": True},
+            "prefill_tok_s": round(prefill_tok_s, 2),
+            "step_bytes": int(alg_step),
+            "step_roofline_frac": round(alg_step / (ms_max / args.steps * 1e-3) / 1e9 / peak, 4),
+            "roofline": dict(roof, peak_kind=peak_kind) if roof else None,
+            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
+                    "api": "xq_decode_one"},
+            "gpu_launches": kernels_per_step * args.steps,
+            "clocks": clk.summary(),
+            "tokens_head": [int(v) for v in toks[:8]],
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline(d, args.cpu_steps)
+        print(json.dumps(line), flush=True)
+    sess.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -116,6 +116,12 @@ XQ_API xq_status xq_create_cuda(const char* model_dir,
                                 const xq_cuda_options* cuda_options,
                                 xq_session** out_session);
 
+/* Run n greedy decode steps back to back on the session's CUDA stream (one graph launch
+ * each, no host round trip between steps) and report their device time from CUDA events
+ * recorded on that stream. tokens (optional, capacity >= n) receives the sampled ids.
+ * Session metrics advance as for n xq_decode_one calls. */
+XQ_API xq_status xq_cuda_decode_timed(xq_session* session, size_t n, int32_t* tokens, double* device_ms);
+
 #ifdef __cplusplus
 }
 #endif

@@ -29,7 +29,7 @@ XQ_ERR_BUFFER_TOO_SMALL = -5
 ABI_SYMBOLS = [
     "xq_create", "xq_destroy", "xq_prefill", "xq_decode_one", "xq_generate", "xq_reset",
     "xq_get_last_metrics", "xq_get_backend_info", "xq_get_kernel_trace_json", "xq_get_debug_json",
-    "xq_get_hidden_state", "xq_run_vulkan_w4a16_selftest", "xq_create_cuda",
+    "xq_get_hidden_state", "xq_run_vulkan_w4a16_selftest", "xq_create_cuda", "xq_cuda_decode_timed",
 ]
 KERNEL_SYMBOLS = [
     "xqk_last_error", "xqk_matrix_create", "xqk_matrix_destroy", "xqk_matrix_info", "xqk_gemv_w4a16",
@@ -90,6 +90,7 @@ def lib():
         getattr(L, n).argtypes = [P, C.c_char_p, C.c_size_t]
     L.xq_get_hidden_state.argtypes = [P, C.POINTER(C.c_float), C.c_size_t, C.POINTER(C.c_size_t)]
     L.xq_run_vulkan_w4a16_selftest.argtypes = [C.c_char_p, C.c_size_t]
+    L.xq_cuda_decode_timed.argtypes = [P, C.c_size_t, C.POINTER(C.c_int32), C.POINTER(C.c_double)]
     L.xqk_last_error.restype = C.c_char_p
     L.xqk_matrix_create.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(P)]
     L.xqk_matrix_destroy.argtypes = [P]
@@ -216,6 +217,21 @@ class Session:
         if st != XQ_OK:
             raise RuntimeError(f"xq_generate failed: {st} {m.error.decode()}")
         return out, m
+
+    def decode_timed(self, n: int, want_tokens: bool = False):
+        """n decode steps back to back; returns (device_ms, tokens or None)."""
+        ms = C.c_double()
+        toks = np.zeros(max(1, n), np.int32) if want_tokens else None
+        ptr = toks.ctypes.data_as(C.POINTER(C.c_int32)) if want_tokens else None
+        st = self.L.xq_cuda_decode_timed(self.h, n, ptr, C.byref(ms))
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_cuda_decode_timed failed: {st}")
+        return ms.value, (toks[:n] if want_tokens else None)
+
+    def metrics(self) -> XqMetrics:
+        m = self._m()
+        self.L.xq_get_last_metrics(self.h, C.byref(m))
+        return m
 
     def hidden(self) -> np.ndarray:
         n = C.c_size_t()

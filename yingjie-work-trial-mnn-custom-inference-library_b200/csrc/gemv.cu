@@ -3,6 +3,7 @@
 #include <cuda_fp16.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <mutex>
@@ -193,34 +194,64 @@ void free_matrix(DevMatrix* m) {
 namespace {
 
 struct Shape {
-    int block, rows_per_chunk, stages, smem;
+    int block, rows_per_chunk, rpt, stages, smem;
 };
 
+// Launch-shape knobs (defaults tuned on B200; the environment overrides exist for sweeps).
+struct Tuning {
+    int block = kTargetBlock;
+    int rpt = 8;
+    int blocks_per_sm = 2;
+    int ring_bytes = kRingBudgetBytes;
+};
+
+const Tuning& tuning() {
+    static const Tuning t = [] {
+        Tuning v;
+        if (const char* e = std::getenv("XQ_GEMV_BLOCK")) v.block = std::max(32, std::min(kMaxBlock, std::atoi(e)));
+        if (const char* e = std::getenv("XQ_GEMV_RPT")) v.rpt = std::atoi(e) >= 8 ? 8 : 4;
+        if (const char* e = std::getenv("XQ_GEMV_BPS")) v.blocks_per_sm = std::max(1, std::min(4, std::atoi(e)));
+        if (const char* e = std::getenv("XQ_GEMV_RING_KB"))
+            v.ring_bytes = std::max(16, std::min(200, std::atoi(e))) * 1024;
+        return v;
+    }();
+    return t;
+}
+
 Shape shape_for(const DevMatrix& m) {
+    const Tuning& tu = tuning();
     Shape s{};
     const int team = m.cols / 32;
-    const int teams = std::max(1, kTargetBlock / team);
+    const int teams = std::max(1, tu.block / team);
     s.block = teams * team;
-    int r = std::min(kMaxRowsPerChunk, teams * kMaxRowsPerTeam);
+    s.rpt = tu.rpt;
+    int r = std::min(kMaxRowsPerChunk, teams * s.rpt);
     r = std::min(r, std::max(2, kStageTargetBytes / m.row_stride));
     r &= ~1;
     s.rows_per_chunk = std::max(2, r);
     const int stage_bytes = s.rows_per_chunk * m.row_stride;
-    s.stages = std::max(2, std::min(kMaxStages, kRingBudgetBytes / stage_bytes));
+    s.stages = std::max(2, std::min(kMaxStages, tu.ring_bytes / stage_bytes));
     s.smem = kGemvHeaderBytes + s.stages * stage_bytes;
     return s;
 }
 
 template <int META, int PRO, int EPI>
 cudaError_t launch_one(const GemvParams& p, dim3 grid, const Shape& s, const LaunchCtx& ctx) {
-    return launch_ex(gemv_w4a16_kernel<META, PRO, EPI>, grid, dim3(s.block), static_cast<size_t>(s.smem),
+    if (s.rpt == 8)
+        return launch_ex(gemv_w4a16_kernel<META, PRO, EPI, 8>, grid, dim3(s.block), static_cast<size_t>(s.smem),
+                         ctx.stream, ctx.pdl, p);
+    return launch_ex(gemv_w4a16_kernel<META, PRO, EPI, 4>, grid, dim3(s.block), static_cast<size_t>(s.smem),
                      ctx.stream, ctx.pdl, p);
 }
 
 template <int META, int PRO, int EPI>
 cudaError_t set_smem() {
-    return cudaFuncSetAttribute(gemv_w4a16_kernel<META, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                kGemvHeaderBytes + kRingBudgetBytes + 2 * kStageTargetBytes);
+    const int bytes = 220 * 1024;  // below the 227 KB opt-in limit, leaving room for static smem
+    cudaError_t e = cudaFuncSetAttribute(gemv_w4a16_kernel<META, PRO, EPI, 4>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(gemv_w4a16_kernel<META, PRO, EPI, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                bytes);
 }
 
 // The (prologue, epilogue) pairs the runtime and the C ABI use.
@@ -246,7 +277,7 @@ bool gemv_init_device() {
 }
 
 int gemv_grid(const DevMatrix& m, int unit, int num_sms, int max_blocks) {
-    int g = std::min(num_sms, m.rows / unit);
+    int g = std::min(num_sms * tuning().blocks_per_sm, m.rows / unit);
     if (max_blocks > 0) g = std::min(g, max_blocks);
     return std::max(1, g);
 }
@@ -503,7 +534,7 @@ int xqk_gemv_w4a16_argmax(const xqk_matrix* m, const float* x_dev, int32_t* inde
     ctx.stream = s;
     ctx.num_sms = m->num_sms;
     ctx.pdl = false;
-    return xqb::launch_gemv(m->m, xqb::kProPlain, xqb::kEpiArgmax, p, 1, ctx) ? 0 : -4;
+    return xqb::launch_gemv(m->m, xqb::kProPlain, xqb::kEpiArgmax, p, 1, ctx, m->num_sms) ? 0 : -4;
 }
 
 }  // extern "C"

@@ -29,11 +29,11 @@ enum Epilogue : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiglu = 2, kEpiConv 
 
 constexpr int kMaxStages = 8;
 constexpr int kMaxRowsPerChunk = 16;
-constexpr int kMaxRowsPerTeam = 4;
+constexpr int kMaxRowsPerTeam = 8;
 constexpr int kMaxBlock = 512;          // K = 16384 needs 512 threads for one team
 constexpr int kTargetBlock = 256;       // leaves room for the next kernel's block (PDL)
 constexpr int kStageTargetBytes = 32 * 1024;
-constexpr int kRingBudgetBytes = 96 * 1024;
+constexpr int kRingBudgetBytes = 64 * 1024;  // 2 blocks/SM + one of the next kernel
 constexpr int kGemvHeaderBytes = 4352;  // mbarriers + warp sums + double-buffered row sums
 
 struct GemvParams {
@@ -72,24 +72,29 @@ struct GemvParams {
     unsigned* err;
 };
 
-// Transpose-reduce 4 per-lane values across a warp: lanes with (lane & 7) == 0 return the
-// warp total of value (lane >> 3).
-__device__ __forceinline__ float reduce4_rows(const float (&p)[4], int lane) {
-    const bool h16 = lane & 16;
-    float k0 = h16 ? p[2] : p[0];
-    float k1 = h16 ? p[3] : p[1];
-    const float s0 = h16 ? p[0] : p[2];
-    const float s1 = h16 ? p[1] : p[3];
-    k0 += __shfl_xor_sync(0xffffffffu, s0, 16);
-    k1 += __shfl_xor_sync(0xffffffffu, s1, 16);
-    const bool h8 = lane & 8;
-    float k = h8 ? k1 : k0;
-    const float s = h8 ? k0 : k1;
-    k += __shfl_xor_sync(0xffffffffu, s, 8);
-    k += __shfl_xor_sync(0xffffffffu, k, 4);
-    k += __shfl_xor_sync(0xffffffffu, k, 2);
-    k += __shfl_xor_sync(0xffffffffu, k, 1);
-    return k;
+// Transpose-reduce N (power of two, <= 32) per-lane values across a warp: afterwards the
+// lanes with (lane % (32 / N)) == 0 hold the warp total of value lane / (32 / N). Each
+// halving step exchanges half of the remaining values (N - 1 shuffles), then the survivors
+// finish with log2(32 / N) butterfly steps.
+template <int N>
+__device__ __forceinline__ float reduce_rows(const float (&p)[N], int lane) {
+    float v[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) v[i] = p[i];
+#pragma unroll
+    for (int n = N, off = 16; n > 1; n >>= 1, off >>= 1) {
+        const bool hi = lane & off;
+#pragma unroll
+        for (int i = 0; i < n / 2; ++i) {
+            const float keep = hi ? v[n / 2 + i] : v[i];
+            const float send = hi ? v[i] : v[n / 2 + i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+    float r = v[0];
+#pragma unroll
+    for (int off = 16 / N; off > 0; off >>= 1) r += __shfl_xor_sync(0xffffffffu, r, off);
+    return r;
 }
 
 __device__ __forceinline__ void argmax_merge(float& bv, int& bi, float v, int i) {
@@ -99,7 +104,7 @@ __device__ __forceinline__ void argmax_merge(float& bv, int& bi, float v, int i)
     }
 }
 
-template <int META, int PRO, int EPI>
+template <int META, int PRO, int EPI, int RPT>
 __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem);                 // kMaxStages mbarriers
@@ -252,44 +257,55 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
         const int nr = min(R, r_end - row0);
         mbar_wait_bounded(&bar[s], static_cast<uint32_t>((ci / nst) & 1), p.err);
         const uint8_t* sb = stages + s * stage_bytes;
-        float part[kMaxRowsPerTeam];
+        // Branch-free over the team's rows (a clamped row index and a predicated result), so
+        // the compiler can overlap the shared loads and dp4a chains of all RPT rows.
+        uint4 wv[RPT];
+        float sc[RPT], off[RPT];
 #pragma unroll
-        for (int jj = 0; jj < kMaxRowsPerTeam; ++jj) {
-            const int j = team + jj * teams;
-            part[jj] = 0.0f;
-            if (j < nr) {
-                const uint8_t* row = sb + j * p.row_stride;
-                const uint4 w = ld_shared_v4(row + 16 * t);
-                const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-                int ae[3] = {acc_init[0], acc_init[1], acc_init[2]};
-                int ao[3] = {0, 0, 0};
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint32_t lw = ws[i] & 0x0F0F0F0Fu;
-                    const uint32_t hw = ws[i] & 0xF0F0F0F0u;
-#pragma unroll
-                    for (int l = 0; l < 3; ++l) {
-                        ae[l] = dp4a_us(lw, le[i][l], ae[l]);
-                        ao[l] = dp4a_us(hw, lo[i][l], ao[l]);
-                    }
-                }
-                const float d2 = static_cast<float>(ae[2] * 16 + ao[2]);
-                const float d1 = static_cast<float>(ae[1] * 16 + ao[1]);
-                const float d0 = static_cast<float>(ae[0] * 16 + ao[0]);
-                const float dot = d2 * 65536.0f + (d1 * 256.0f + d0);
-                if constexpr (META == kMetaSym16) {
-                    const float sc = __half2float(*reinterpret_cast<const __half*>(row + p.meta_offset + 2 * (t >> 1)));
-                    part[jj] = dot * (sc * down) + nan_or_zero;
-                } else {
-                    const float2 sbv = *reinterpret_cast<const float2*>(row + p.meta_offset + 8 * (t >> 1));
-                    part[jj] = dot * (sbv.x * down) + sbv.y * xsum + nan_or_zero;
-                }
+        for (int jj = 0; jj < RPT; ++jj) {
+            const int jc = min(team + jj * teams, nr - 1);
+            const uint8_t* row = sb + jc * p.row_stride;
+            wv[jj] = ld_shared_v4(row + 16 * t);
+            if constexpr (META == kMetaSym16) {
+                sc[jj] = __half2float(*reinterpret_cast<const __half*>(row + p.meta_offset + 2 * (t >> 1)));
+                off[jj] = 0.0f;
+            } else {
+                const float2 sbv = *reinterpret_cast<const float2*>(row + p.meta_offset + 8 * (t >> 1));
+                sc[jj] = sbv.x;
+                off[jj] = sbv.y;
             }
         }
-        const float v = reduce4_rows(part, lane);
+        float part[RPT];
+#pragma unroll
+        for (int jj = 0; jj < RPT; ++jj) {
+            const uint32_t ws[4] = {wv[jj].x, wv[jj].y, wv[jj].z, wv[jj].w};
+            int ae[3] = {acc_init[0], acc_init[1], acc_init[2]};
+            int ao[3] = {0, 0, 0};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t lw = ws[i] & 0x0F0F0F0Fu;
+                const uint32_t hw = ws[i] & 0xF0F0F0F0u;
+#pragma unroll
+                for (int l = 0; l < 3; ++l) {
+                    ae[l] = dp4a_us(lw, le[i][l], ae[l]);
+                    ao[l] = dp4a_us(hw, lo[i][l], ao[l]);
+                }
+            }
+            const float d2 = static_cast<float>(ae[2] * 16 + ao[2]);
+            const float d1 = static_cast<float>(ae[1] * 16 + ao[1]);
+            const float d0 = static_cast<float>(ae[0] * 16 + ao[0]);
+            const float dot = d2 * 65536.0f + (d1 * 256.0f + d0);
+            float val;
+            if constexpr (META == kMetaSym16)
+                val = dot * (sc[jj] * down) + nan_or_zero;
+            else
+                val = dot * (sc[jj] * down) + off[jj] * xsum + nan_or_zero;
+            part[jj] = (team + jj * teams < nr) ? val : 0.0f;
+        }
+        const float v = reduce_rows<RPT>(part, lane);
         float* rbuf = red + (ci & 1) * (kMaxRowsPerChunk * 32);
-        if ((lane & 7) == 0) {
-            const int j = team + (lane >> 3) * teams;
+        if ((lane & (32 / RPT - 1)) == 0) {
+            const int j = team + (lane / (32 / RPT)) * teams;
             if (j < nr) rbuf[j * 32 + wit] = v;
         }
         __syncthreads();

@@ -138,6 +138,7 @@ DeviceModel::~DeviceModel() {
         cudaFree(L.v_cache);
     }
     free_matrix(&lm_head_);
+    cudaFree(d_rope_);
     for (void* p : allocs_) cudaFree(p);
     if (h_token_) cudaFreeHost(h_token_);
     if (stream_) cudaStreamDestroy(stream_);
@@ -391,6 +392,16 @@ bool DeviceModel::alloc_kv(int capacity, std::string* error) {
         L.v_cache = v;
         device_bytes_ += 2 * per_pos * capacity;
     }
+    // RoPE table for every position the cache can hold.
+    std::vector<float2> rope;
+    rope_table(0, capacity, d_.rotary_dim, d_.theta, &rope);
+    if (d_rope_) cudaFree(d_rope_);
+    d_rope_ = nullptr;
+    if (cudaMalloc(&d_rope_, rope.size() * sizeof(float2)) != cudaSuccess ||
+        cudaMemcpy(d_rope_, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess) {
+        *error = "rope table upload failed";
+        return false;
+    }
     capacity_ = capacity;
     return true;
 }
@@ -473,6 +484,8 @@ bool DeviceModel::enqueue_forward(cudaStream_t s) {
             ap.rotary = d.rotary_dim;
             ap.theta = d.theta;
             ap.eps = d.eps;
+            ap.rope = d_rope_;
+            ap.rope_stride = d.rotary_dim / 2;
             ap.part = d_attn_part_;
             ap.counters = d_attn_counters_;
             ap.out = d_attn_out_;
@@ -671,6 +684,31 @@ bool DeviceModel::decode_many(size_t count, std::string* error) {
     cudaSetDevice(opts_.device);
     for (size_t i = 0; i < count; ++i)
         if (!run_step(true, error)) return false;
+    return true;
+}
+
+bool DeviceModel::decode_many_timed(size_t count, double* device_ms, std::string* error) {
+    cudaSetDevice(opts_.device);
+    // Capture (or re-capture after growth) before the first event so it is not timed.
+    if (!ensure_capacity(position_ + static_cast<int>(count), error)) return false;
+    if (opts_.use_graphs && !g_decode_ && !capture_graphs(error)) return false;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, stream_);
+    const bool ok = decode_many(count, error);
+    cudaEventRecord(e1, stream_);
+    const cudaError_t e = cudaEventSynchronize(e1);
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (!ok) return false;
+    if (e != cudaSuccess) {
+        *error = std::string("decode failed: ") + cudaGetErrorString(e);
+        return false;
+    }
+    *device_ms = ms;
     return true;
 }
 

@@ -68,6 +68,8 @@ public:
     // Enqueue `count` decode steps without host synchronisation; tokens land in the ring.
     bool decode_many(size_t count, std::string* error);
     bool read_ring(size_t first, size_t count, int32_t* out, std::string* error);
+    // decode_many bracketed by CUDA events on the model stream; returns device milliseconds.
+    bool decode_many_timed(size_t count, double* device_ms, std::string* error);
     // Post-final-norm hidden state (what copyHidden returns, custom_model.cpp:1438-1447).
     bool hidden(std::vector<float>* out, std::string* error);
     // Full lm_head logits of the current (normed) hidden state, for debug JSON.
@@ -121,6 +123,7 @@ private:
     float* d_arg_val_ = nullptr;
     int* d_arg_idx_ = nullptr;
     unsigned* d_arg_counter_ = nullptr;
+    float2* d_rope_ = nullptr;  // [capacity][rotary/2] (cos, sin), rebuilt when the KV cache grows
     float* d_attn_part_ = nullptr;
     unsigned* d_attn_counters_ = nullptr;
     unsigned* d_err_ = nullptr;

@@ -130,7 +130,7 @@ __device__ __forceinline__ void kv_st(__half* p, float v) { *p = __float2half_rn
 // RoPE (applyRopeVector, :351-370) on one head held as v[m] = x[lane + 32 m]. The rotated
 // pairs (i, 32 + i), i < 32, are v[0], v[1] of lane i (rotary_dim = 64).
 __device__ __forceinline__ void norm_rope_head(float (&v)[8], const float* w, int hd, float eps, int lane,
-                                               int pos, int rotary, float theta) {
+                                               const float2* rope_row) {
     float ss = 0.0f;
 #pragma unroll
     for (int m = 0; m < 8; ++m) ss += v[m] * v[m];
@@ -138,9 +138,8 @@ __device__ __forceinline__ void norm_rope_head(float (&v)[8], const float* w, in
     const float inv = 1.0f / sqrtf(ss / static_cast<float>(hd) + eps);
 #pragma unroll
     for (int m = 0; m < 8; ++m) v[m] *= inv * w[lane + 32 * m];
-    const float inv_freq = powf(theta, -static_cast<float>(2 * lane) / static_cast<float>(rotary));
-    const float angle = static_cast<float>(pos) * inv_freq;
-    const float c = cosf(angle), s = sinf(angle);
+    const float2 cs = rope_row[lane];
+    const float c = cs.x, s = cs.y;
     const float x0 = v[0], x1 = v[1];
     v[0] = x0 * c - x1 * s;
     v[1] = x1 * c + x0 * s;
@@ -173,13 +172,14 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     const int t0 = min(L, split * chunk);
     const int t1 = min(L, t0 + chunk);
     const int n = t1 - t0;
+    const float2* rope_row = p.rope + static_cast<size_t>(p.rope_stride) * pos;
 
     if (warp < group) {  // query head kh*group + warp: [query | gate] split (custom_model.cpp:740-753)
         const float* src = p.qkv + static_cast<size_t>(kh * group + warp) * 2 * hd;
         float v[8];
 #pragma unroll
         for (int m = 0; m < 8; ++m) v[m] = src[lane + 32 * m];
-        norm_rope_head(v, p.q_norm, hd, p.eps, lane, pos, p.rotary, p.theta);
+        norm_rope_head(v, p.q_norm, hd, p.eps, lane, rope_row);
 #pragma unroll
         for (int m = 0; m < 8; ++m) qs[warp * hd + lane + 32 * m] = v[m];
     }
@@ -190,7 +190,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         float v[8];
 #pragma unroll
         for (int m = 0; m < 8; ++m) v[m] = ks[lane + 32 * m];
-        norm_rope_head(v, p.k_norm, hd, p.eps, lane, pos, p.rotary, p.theta);
+        norm_rope_head(v, p.k_norm, hd, p.eps, lane, rope_row);
         KV* kd = kc + (static_cast<size_t>(pos) * p.nkv + kh) * hd;
         KV* vd = vc + (static_cast<size_t>(pos) * p.nkv + kh) * hd;
 #pragma unroll
@@ -290,6 +290,18 @@ cudaError_t attention_init_device(int max_smem_bytes) {
     return cudaFuncSetAttribute(attention_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem_bytes);
 }
 
+void rope_table(int first, int count, int rotary, float theta, std::vector<float2>* out) {
+    const int half = rotary / 2;
+    out->resize(static_cast<size_t>(count) * half);
+    for (int i = 0; i < half; ++i) {
+        const float inv_freq = std::pow(theta, -static_cast<float>(2 * i) / static_cast<float>(rotary));
+        for (int p = 0; p < count; ++p) {
+            const float angle = static_cast<float>(first + p) * inv_freq;
+            (*out)[static_cast<size_t>(p) * half + i] = make_float2(std::cos(angle), std::sin(angle));
+        }
+    }
+}
+
 size_t attention_smem_bytes(int nq, int nkv, int hd, int capacity) {
     const int group = nq / nkv;
     return static_cast<size_t>(group) * (hd + (capacity + kAttnSplits - 1) / kAttnSplits) * sizeof(float);
@@ -337,6 +349,7 @@ namespace {
 struct AttnScratch {
     float* part = nullptr;
     unsigned* counters = nullptr;
+    float2* rope = nullptr;
     size_t part_floats = 0;
     int nkv = 0;
 };
@@ -386,6 +399,7 @@ int xqk_attention_step(const float* qkv_dev, const float* q_norm_dev, const floa
         cudaFree(s.counters);
         if (cudaMalloc(&s.part, need * sizeof(float)) != cudaSuccess ||
             cudaMalloc(&s.counters, nkv * sizeof(unsigned)) != cudaSuccess ||
+            (!s.rope && cudaMalloc(&s.rope, 512 * sizeof(float2)) != cudaSuccess) ||
             cudaMemset(s.counters, 0, nkv * sizeof(unsigned)) != cudaSuccess) {
             s = AttnScratch();
             xqb::set_last_error("xqk_attention_step: scratch allocation failed");
@@ -412,6 +426,15 @@ int xqk_attention_step(const float* qkv_dev, const float* q_norm_dev, const floa
     p.part = s.part;
     p.counters = s.counters;
     p.out = out_dev;
+    std::vector<float2> rope;
+    xqb::rope_table(position, 1, rotary_dim, theta, &rope);
+    if (cudaMemcpyAsync(s.rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice,
+                        static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+        xqb::set_last_error("xqk_attention_step: rope upload failed");
+        return -4;
+    }
+    p.rope = s.rope;
+    p.rope_stride = 0;
     const size_t smem = xqb::attention_smem_bytes(nq, nkv, hd, capacity);
     if (smem > 200 * 1024) {
         xqb::set_last_error("xqk_attention_step: capacity too large for one call");

@@ -2,6 +2,8 @@
 // attention, embedding row load, RMSNorm.
 #pragma once
 
+#include <vector>
+
 #include "common.cuh"
 
 namespace xqb {
@@ -38,6 +40,8 @@ struct AttnParams {
     int pos_const;
     int nq, nkv, hd, rotary;
     float theta, eps;
+    const float2* rope;   // (cos, sin) of position * inv_freq[i], i < rotary/2, per position
+    int rope_stride;      // floats2 per position row; 0: a single row for this call's position
     float* part;          // [nkv][kAttnSplits][group][hd + 2]
     unsigned* counters;   // [nkv]
     float* out;           // [nq*hd]
@@ -48,6 +52,10 @@ struct AttnParams {
 cudaError_t launch_attention(const AttnParams& p, bool kv_fp16, size_t smem, cudaStream_t s, bool pdl);
 cudaError_t attention_init_device(int max_smem_bytes);
 size_t attention_smem_bytes(int nq, int nkv, int hd, int capacity);
+// Host-side RoPE table with the reference's arithmetic (applyRopeVector,
+// custom_model.cpp:351-370): inv_freq = pow(theta, -2i/rotary), angle = pos * inv_freq,
+// (cos, sin) in fp32 through the same libm calls, for positions [first, first + count).
+void rope_table(int first, int count, int rotary, float theta, std::vector<float2>* out);
 
 // ---- Small ops ------------------------------------------------------------------------
 // hidden = embedding row of prompt[*next_pos]; *pos = *next_pos; ++*next_pos (prefill step).

@@ -289,6 +289,31 @@ public:
         return XQ_OK;
     }
 
+    xq_status decode_timed(size_t n, int32_t* tokens, double* device_ms) {
+        if (!loaded_ || !has_prefill_) {
+            set_error("decode requires a loaded session and completed prefill");
+            return XQ_ERR_NOT_READY;
+        }
+        if (!device_ms) return XQ_ERR_INVALID_ARGUMENT;
+        std::string err;
+        const size_t first = ring_first();
+        const auto t0 = Clock::now();
+        if (!model_->decode_many_timed(n, device_ms, &err) ||
+            (tokens && n && !model_->read_ring(first, n, tokens, &err))) {
+            set_error(err);
+            return XQ_ERR_RUNTIME;
+        }
+        const double ms = elapsed_ms(t0, Clock::now());
+        trace_decode(n, ms);
+        position_ += n;
+        if (metrics_.generated_tokens == 0 && n) metrics_.first_token_ms = ms / static_cast<double>(n);
+        metrics_.generated_tokens += n;
+        metrics_.decode_total_ms += ms;
+        metrics_.total_generate_ms = metrics_.prefill_ms + metrics_.decode_total_ms;
+        update_rates();
+        return XQ_OK;
+    }
+
     xq_status reset() {  // session.cpp:505-525
         has_prefill_ = false;
         position_ = 0;
@@ -557,6 +582,11 @@ xq_status xq_get_debug_json(xq_session* s, char* b, size_t c) {
 xq_status xq_get_hidden_state(xq_session* s, float* v, size_t cap, size_t* out_size) {
     if (!s || !out_size) return XQ_ERR_INVALID_ARGUMENT;
     return XQ_SESSION(s)->hidden_state(v, cap, out_size);
+}
+
+xq_status xq_cuda_decode_timed(xq_session* s, size_t n, int32_t* tokens, double* device_ms) {
+    if (!s) return XQ_ERR_INVALID_ARGUMENT;
+    return XQ_SESSION(s)->decode_timed(n, tokens, device_ms);
 }
 
 // runVulkanW4A16SelfTestJson on a host without Vulkan (vulkan_backend.cpp:1638-1656).
