@@ -74,6 +74,22 @@ XQK_API int xqk_attention_step(const float* qkv_dev, const float* q_norm_dev, co
                                int nq, int nkv, int hd, int rotary_dim, float theta, float eps, float* out_dev,
                                void* stream);
 
+/* xqk_attention_step without any device allocation. No counterpart in the reference (whose
+ * CPU kernels need no device memory); it exists for callers that cannot call cudaMalloc
+ * while they run: plugin-style hosts that provide every buffer themselves, code under a
+ * fixed device-memory budget, or paths where an allocation would synchronise the device.
+ * Same arguments, arithmetic and results as xqk_attention_step. Its scratch is a 1 MiB
+ * static device array compiled into the library, held by every GPU that loads the library
+ * until the process exits; calls needing more (nkv * 32 * (nq / nkv) * (head_dim + 2) + 128
+ * floats above 262144, or more than 64 kv heads) are rejected with an error. The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress), so make that first
+ * call before any stream capture. All calls share the array: calls that overlap on the GPU
+ * (other streams, other host threads) race and must be serialised by the caller. */
+XQK_API int xqk_attention_step_noalloc(const float* qkv_dev, const float* q_norm_dev, const float* k_norm_dev,
+                                       void* k_cache_dev, void* v_cache_dev, int kv_fp16, int capacity,
+                                       int position, int nq, int nkv, int hd, int rotary_dim, float theta, float eps,
+                                       float* out_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

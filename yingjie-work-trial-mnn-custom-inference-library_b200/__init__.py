@@ -34,7 +34,7 @@ ABI_SYMBOLS = [
 KERNEL_SYMBOLS = [
     "xqk_last_error", "xqk_matrix_create", "xqk_matrix_destroy", "xqk_matrix_info", "xqk_gemv_w4a16",
     "xqk_gemv_w4a16_host", "xqk_gemv_w4a16_argmax", "xqk_rmsnorm", "xqk_gated_delta_step",
-    "xqk_attention_step",
+    "xqk_attention_step", "xqk_attention_step_noalloc",
 ]
 
 
@@ -104,6 +104,7 @@ def lib():
     L.xqk_gated_delta_step.argtypes = [P, P, P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, P]
     L.xqk_attention_step.argtypes = [P, P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                      C.c_int, C.c_float, C.c_float, P, P]
+    L.xqk_attention_step_noalloc.argtypes = L.xqk_attention_step.argtypes
     _lib = L
     return L
 

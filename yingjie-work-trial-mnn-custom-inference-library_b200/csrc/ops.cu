@@ -4,6 +4,8 @@
 
 #include <cmath>
 #include <mutex>
+#include <string>
+#include <vector>
 
 #include "../../include/xq_kernels.h"
 #include "gemv.hpp"
@@ -343,6 +345,15 @@ __global__ void rmsnorm_kernel(const float* x, const float* w, int n, float eps,
 }  // namespace xqb
 
 // ------------------------------------------------------------------------------------
+// Allocation-free attention step: scratch lives in this file-scope device array, which every
+// GPU that loads the library holds until the process exits. 1 MiB per device.
+// ------------------------------------------------------------------------------------
+namespace xqb {
+constexpr size_t kNoAllocScratchFloats = 256 * 1024;
+}  // namespace xqb
+static __device__ __align__(256) float g_attention_noalloc_scratch[xqb::kNoAllocScratchFloats];
+
+// ------------------------------------------------------------------------------------
 // Kernel-level C ABI
 // ------------------------------------------------------------------------------------
 namespace {
@@ -442,6 +453,103 @@ int xqk_attention_step(const float* qkv_dev, const float* q_norm_dev, const floa
     }
     cudaError_t e = xqb::attention_init_device(200 * 1024);
     if (e == cudaSuccess) e = xqb::launch_attention(p, kv_fp16 != 0, smem, static_cast<cudaStream_t>(stream), false);
+    if (e != cudaSuccess) {
+        xqb::set_last_error(std::string("attention launch failed: ") + cudaGetErrorString(e));
+        return -4;
+    }
+    return 0;
+}
+
+// Same contract and arithmetic as xqk_attention_step, for callers that must not allocate
+// device memory while they run (plugin hosts that hand out all buffers themselves, code
+// running under a fixed device-memory budget, or paths where an allocation would
+// synchronise the device). Layout of the static scratch: 32 (cos, sin) RoPE pairs, then one
+// completion counter per kv head, then the per-split partial results.
+int xqk_attention_step_noalloc(const float* qkv_dev, const float* q_norm_dev, const float* k_norm_dev,
+                               void* k_cache_dev, void* v_cache_dev, int kv_fp16, int capacity, int position,
+                               int nq, int nkv, int hd, int rotary_dim, float theta, float eps, float* out_dev,
+                               void* stream) {
+    if (!qkv_dev || !q_norm_dev || !k_norm_dev || !k_cache_dev || !v_cache_dev || !out_dev || nq <= 0 || nkv <= 0 ||
+        position < 0 || position >= capacity)
+        return -1;
+    if (hd != xqb::kAttnThreads || rotary_dim != 64 || nq % nkv != 0 || nq / nkv > xqb::kAttnMaxGroup) {
+        xqb::set_last_error("xqk_attention_step_noalloc: needs head_dim 256, rotary_dim 64, q/kv group <= 8");
+        return -1;
+    }
+    constexpr size_t kRopeFloats = 64, kCounterFloats = 64;
+    const size_t part_floats = static_cast<size_t>(nkv) * xqb::kAttnSplits * (nq / nkv) * (hd + 2);
+    if (nkv > static_cast<int>(kCounterFloats) || kRopeFloats + kCounterFloats + part_floats > xqb::kNoAllocScratchFloats) {
+        xqb::set_last_error("xqk_attention_step_noalloc: needs " +
+                            std::to_string(kRopeFloats + kCounterFloats + part_floats) +
+                            " floats of scratch but the static scratch holds " +
+                            std::to_string(xqb::kNoAllocScratchFloats) + " (at most 64 kv heads and nkv * 32 * "
+                            "group * (head_dim + 2) + 128 floats)");
+        return -1;
+    }
+    const size_t smem = xqb::attention_smem_bytes(nq, nkv, hd, capacity);
+    if (smem > 200 * 1024) {
+        xqb::set_last_error("xqk_attention_step_noalloc: capacity too large for one call");
+        return -1;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        xqb::set_last_error("xqk_attention_step_noalloc: no usable current device");
+        return -4;
+    }
+    // Once per device, with that device current: the device address of the static array
+    // (its name in host code is only a host-side stand-in).
+    static std::mutex mu;
+    static float* base[64] = {};
+    float* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!base[dev]) {
+            void* ptr = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&ptr, g_attention_noalloc_scratch);
+            if (e != cudaSuccess) {
+                xqb::set_last_error(std::string("xqk_attention_step_noalloc: cudaGetSymbolAddress failed: ") +
+                                    cudaGetErrorString(e));
+                return -4;
+            }
+            base[dev] = static_cast<float*>(ptr);
+        }
+        scratch = base[dev];
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float2* rope_dev = reinterpret_cast<float2*>(scratch);
+    unsigned* counters = reinterpret_cast<unsigned*>(scratch + kRopeFloats);
+    float* part = scratch + kRopeFloats + kCounterFloats;
+    std::vector<float2> rope;
+    xqb::rope_table(position, 1, rotary_dim, theta, &rope);
+    // The counters must start at zero; the array keeps whatever the last call left in it.
+    if (cudaMemcpyAsync(rope_dev, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice, st) !=
+            cudaSuccess ||
+        cudaMemsetAsync(counters, 0, static_cast<size_t>(nkv) * sizeof(unsigned), st) != cudaSuccess) {
+        xqb::set_last_error("xqk_attention_step_noalloc: scratch set-up copy failed");
+        return -4;
+    }
+    xqb::AttnParams p = {};
+    p.qkv = qkv_dev;
+    p.q_norm = q_norm_dev;
+    p.k_norm = k_norm_dev;
+    p.k_cache = k_cache_dev;
+    p.v_cache = v_cache_dev;
+    p.capacity = capacity;
+    p.pos_ptr = nullptr;
+    p.pos_const = position;
+    p.nq = nq;
+    p.nkv = nkv;
+    p.hd = hd;
+    p.rotary = rotary_dim;
+    p.theta = theta;
+    p.eps = eps;
+    p.rope = rope_dev;
+    p.rope_stride = 0;
+    p.part = part;
+    p.counters = counters;
+    p.out = out_dev;
+    cudaError_t e = xqb::attention_init_device(200 * 1024);
+    if (e == cudaSuccess) e = xqb::launch_attention(p, kv_fp16 != 0, smem, st, false);
     if (e != cudaSuccess) {
         xqb::set_last_error(std::string("attention launch failed: ") + cudaGetErrorString(e));
         return -4;
