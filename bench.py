@@ -208,6 +208,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--kv-fp16", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=12)
+    ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt length (512 = the benchmark shape)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -228,9 +229,9 @@ def main():
     d = make_package(rank, world)
     if world > 1:
         dist.barrier()
-    sess = pkg.Session(d, device=local, kv_fp16=args.kv_fp16, max_context_tokens=PROMPT_LEN + args.warmup +
+    sess = pkg.Session(d, device=local, kv_fp16=args.kv_fp16, max_context_tokens=args.prompt + args.warmup +
                        args.steps + 128)
-    ids = np.random.default_rng(SEED + rank).integers(0, 248320, PROMPT_LEN).astype(np.int32)
+    ids = np.random.default_rng(SEED + rank).integers(0, 248320, args.prompt).astype(np.int32)
     m = sess.prefill(ids)
     prefill_tok_s = m.prefill_tokens_per_second
     sess.decode_timed(args.warmup)  # untimed warm-up steps (graph capture happens here)
@@ -265,7 +266,7 @@ def main():
     roof = gemv_roofline(pkg, peak) if rank == 0 else None
     step_bytes = info.get("weight_bytes", 0)
     if rank == 0:
-        ctx0 = PROMPT_LEN + args.warmup
+        ctx0 = args.prompt + args.warmup
         kv_elem = 2 if args.kv_fp16 else 4
         kv_bytes = 8 * 2 * 4 * 256 * kv_elem * (ctx0 + args.steps / 2)  # mean context over the timed steps
         state_bytes = 24 * (2 * 32 * 128 * 128 * 4 + 2 * 8192 * 3 * 4)
@@ -277,8 +278,8 @@ def main():
             "data": "synthetic (seeded random-init 9B-shaped package)",
             "config": {"workload": "config2: Qwen3.5-9B-shaped W4A16 g64 (32 layers, 3:1 DeltaNet:GQA, vocab "
                                    "248320), 512-token random prompt, greedy decode, batch 1",
-                       "prompt": PROMPT_LEN, "context_during_timing": [PROMPT_LEN + args.warmup,
-                                                                        PROMPT_LEN + args.warmup + args.steps],
+                       "prompt": args.prompt, "context_during_timing": [args.prompt + args.warmup,
+                                                                         args.prompt + args.warmup + args.steps],
                        "kv_dtype": "f16" if args.kv_fp16 else "f32", "parallelism": f"replicas{world}",
                        "l2": "inputs larger than L2 (4.3 GB of weights streamed per step)",
                        "cuda_graphs": True, "pdl": True},

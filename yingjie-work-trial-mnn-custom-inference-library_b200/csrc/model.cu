@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <fstream>
 #include <sstream>
@@ -426,12 +427,23 @@ int DeviceModel::kernels_per_decode_step() const {
 
 int DeviceModel::kernels_per_prefill_step() const { return kernels_per_decode_step(); }
 
+// Programmatic dependent launch between the kernels of a step (XQ_PDL=0 turns it off, for
+// A/B measurements).
+static bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("XQ_PDL");
+        return !(e && std::atoi(e) == 0);
+    }();
+    return on;
+}
+
 bool DeviceModel::enqueue_forward(cudaStream_t s) {
     const ModelDims& d = d_;
+    const bool pdl = pdl_enabled();
     LaunchCtx ctx;
     ctx.stream = s;
     ctx.num_sms = num_sms_;
-    ctx.pdl = true;
+    ctx.pdl = pdl;
     for (DevLayer& L : layers_) {
         if (!L.full) {
             GemvParams p = {};
@@ -448,7 +460,7 @@ bool DeviceModel::enqueue_forward(cudaStream_t s) {
             if (!launch_gemv(L.in_proj, kProRms, kEpiConv, p, 1, ctx)) return false;
             DeltaParams dp{d_conv_out_, d_zab_ + d.lv_dim, L.a_log, L.dt_bias, L.rec_state, d_attn_raw_,
                            d.lk_heads, d.lv_heads, d.lk_hd, d.lv_hd};
-            if (launch_ex(gated_delta_kernel, dim3(d.lv_heads, d.lv_hd / kDeltaCols), dim3(d.lk_hd), 0, s, true,
+            if (launch_ex(gated_delta_kernel, dim3(d.lv_heads, d.lv_hd / kDeltaCols), dim3(d.lk_hd), 0, s, pdl,
                           dp) != cudaSuccess) {
                 set_last_error("gated delta launch failed");
                 return false;
@@ -491,7 +503,7 @@ bool DeviceModel::enqueue_forward(cudaStream_t s) {
             ap.out = d_attn_out_;
             ap.err = d_err_;
             const size_t smem = attention_smem_bytes(d.heads, d.kv_heads, d.head_dim, capacity_);
-            const cudaError_t e = launch_attention(ap, opts_.kv_fp16, smem, s, true);
+            const cudaError_t e = launch_attention(ap, opts_.kv_fp16, smem, s, pdl);
             if (e != cudaSuccess) {
                 set_last_error(std::string("attention launch failed: ") + cudaGetErrorString(e));
                 return false;
@@ -522,7 +534,7 @@ bool DeviceModel::enqueue_decode_step(cudaStream_t s) {
     LaunchCtx ctx;
     ctx.stream = s;
     ctx.num_sms = num_sms_;
-    ctx.pdl = true;
+    ctx.pdl = pdl_enabled();
     GemvParams p = {};
     p.x = d_hidden_;
     p.norm_w = d_final_norm_;  // runFinalNorm, custom_model.cpp:1258-1279
@@ -545,7 +557,7 @@ bool DeviceModel::enqueue_decode_step(cudaStream_t s) {
 }
 
 bool DeviceModel::enqueue_prefill_step(cudaStream_t s) {
-    if (launch_ex(embed_prefill_kernel, dim3(1), dim3(512), 0, s, true, static_cast<const int*>(d_prompt_),
+    if (launch_ex(embed_prefill_kernel, dim3(1), dim3(512), 0, s, pdl_enabled(), static_cast<const int*>(d_prompt_),
                   static_cast<const uint16_t*>(d_emb_), d_hidden_, d_.hidden, d_.vocab, d_pos_, d_next_pos_) !=
         cudaSuccess) {
         set_last_error("embedding launch failed");
