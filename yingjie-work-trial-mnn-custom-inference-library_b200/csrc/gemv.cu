@@ -222,11 +222,10 @@ Shape shape_for(const DevMatrix& m) {
     const Tuning& tu = tuning();
     Shape s{};
     const int team = m.cols / 32;
-    const int teams = std::max(1, tu.block / team);
-    s.block = teams * team;
+    const int teams = std::max(1, std::min((kMaxBlock - 32) / team, tu.block / team));
+    s.block = teams * team + 32;  // + producer warp
     s.rpt = tu.rpt;
-    int r = std::min(kMaxRowsPerChunk, teams * s.rpt);
-    r = std::min(r, std::max(2, kStageTargetBytes / m.row_stride));
+    int r = std::min(s.rpt, std::max(2, kStageTargetBytes / m.row_stride));
     r &= ~1;
     s.rows_per_chunk = std::max(2, r);
     const int stage_bytes = s.rows_per_chunk * m.row_stride;

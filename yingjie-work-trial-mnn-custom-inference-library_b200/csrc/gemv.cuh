@@ -13,10 +13,11 @@
 // [32t, 32t+32) = nibble bytes [16t, 16t+16) and half of group t/2. x never changes while
 // rows stream past, so each thread keeps its 32 x values in registers as three signed
 // 8-bit limbs of a 22-bit fixed-point mantissa (scale 2^S per thread chunk); the code * x
-// products then run as exact integer dp4a sums, converted to fp32 once per row. Rows reach
-// shared memory through a `stages`-deep ring of 1-D bulk async copies (cp.async.bulk +
-// mbarrier). The first `stages` copies are issued BEFORE griddepcontrol.wait: weights do not
-// depend on the previous kernel, so their streaming overlaps that kernel's tail.
+// products then run as exact integer dp4a sums, converted to fp32 once per row. A producer
+// warp streams row chunks into a `stages`-deep shared-memory ring with 1-D bulk async copies
+// (cp.async.bulk + full/empty mbarriers); it never waits on the previous kernel
+// (griddepcontrol.wait is only in the consumers), so with programmatic dependent launch the
+// weight streaming of a kernel overlaps the tail of the one before it.
 #pragma once
 
 #include "common.cuh"
@@ -27,14 +28,14 @@ enum MetaKind : int { kMetaSym16 = 0, kMetaAff32 = 1 };
 enum Prologue : int { kProPlain = 0, kProRms = 1, kProGatedRms = 2 };
 enum Epilogue : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiglu = 2, kEpiConv = 3, kEpiArgmax = 4 };
 
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 16;
 constexpr int kMaxRowsPerChunk = 16;
 constexpr int kMaxRowsPerTeam = 8;
-constexpr int kMaxBlock = 512;          // K = 16384 needs 512 threads for one team
-constexpr int kTargetBlock = 256;       // leaves room for the next kernel's block (PDL)
+constexpr int kMaxBlock = 544;           // K = 16384: one 512-thread team + the producer warp
+constexpr int kTargetBlock = 256;       // consumer threads per block (plus one producer warp)
 constexpr int kStageTargetBytes = 32 * 1024;
-constexpr int kRingBudgetBytes = 64 * 1024;  // 2 blocks/SM + one of the next kernel
-constexpr int kGemvHeaderBytes = 4352;  // mbarriers + warp sums + double-buffered row sums
+constexpr int kRingBudgetBytes = 96 * 1024;
+constexpr int kGemvHeaderBytes = 4608;  // full/empty mbarriers, warp sums, double-buffered row sums
 
 struct GemvParams {
     const uint8_t* w;  // device rows
@@ -104,22 +105,33 @@ __device__ __forceinline__ void argmax_merge(float& bv, int& bi, float v, int i)
     }
 }
 
+__device__ __forceinline__ void named_bar(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Block = `teams` consumer teams of K/32 threads + one producer warp (the last warp).
+// The producer streams this block's row chunks into a ring of shared-memory stages with
+// 1-D bulk copies (full[s] completes when a stage has landed, empty[s] when its team has
+// read it). Consumer team `t` owns chunks t, t + teams, ... and synchronises only within
+// the team (named barrier 2 + t), so teams never wait for each other.
 template <int META, int PRO, int EPI, int RPT>
 __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);                 // kMaxStages mbarriers
-    float* wsum = reinterpret_cast<float*>(smem + 64);                  // 32 floats
-    float* red = reinterpret_cast<float*>(smem + 256);                  // [2][16][32]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kMaxStages;
+    float* wsum = reinterpret_cast<float*>(smem + 256);  // one float per warp
+    float* red = reinterpret_cast<float*>(smem + 512);   // [2][kMaxRowsPerChunk][32 warps]
     uint8_t* stages = smem + kGemvHeaderBytes;
 
     const int tid = threadIdx.x;
     const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int consumers = blockDim.x - 32;
     const int team_size = p.cols >> 5;
-    const int teams = blockDim.x / team_size;
-    const int team = tid / team_size;
-    const int t = tid - team * team_size;
-    const int wpt = team_size >> 5;       // warps per team
-    const int wit = t >> 5;               // warp index inside the team
+    const int teams = consumers / team_size;
     const int R = p.rows_per_chunk;
     const int nst = p.stages;
     const int stage_bytes = R * p.row_stride;
@@ -129,24 +141,35 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
     const int r_end = static_cast<int>((long long)units * (blockIdx.x + 1) / gridDim.x) * p.unit;
     const int nchunks = (r_end - r_begin + R - 1) / R;
 
-    auto issue = [&](int ci) {
-        const int s = ci % nst;
-        const int row0 = r_begin + ci * R;
-        const int nr = min(R, r_end - row0);
-        const uint32_t bytes = static_cast<uint32_t>(nr * p.row_stride);
-        mbar_expect_tx(&bar[s], bytes);
-        bulk_g2s(stages + s * stage_bytes, p.w + static_cast<size_t>(row0) * p.row_stride, bytes, &bar[s]);
-    };
-
     if (tid == 0) {
-        for (int s = 0; s < nst; ++s) mbar_init(&bar[s], 1);
+        for (int s = 0; s < nst; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
         fence_mbar_init();
     }
     __syncthreads();
-    if (tid == 0) {
-        for (int ci = 0; ci < nst && ci < nchunks; ++ci) issue(ci);
-    }
     pdl_launch_dependents();
+
+    if (warp == (consumers >> 5)) {
+        // Producer: weights never depend on the previous kernel, so no griddepcontrol.wait.
+        if (lane == 0) {
+            for (int ci = 0; ci < nchunks; ++ci) {
+                const int s = ci % nst;
+                if (ci >= nst) mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((ci / nst) - 1) & 1), p.err);
+                const int row0 = r_begin + ci * R;
+                const uint32_t bytes = static_cast<uint32_t>(min(R, r_end - row0) * p.row_stride);
+                mbar_expect_tx(&full[s], bytes);
+                bulk_g2s(stages + s * stage_bytes, p.w + static_cast<size_t>(row0) * p.row_stride, bytes, &full[s]);
+            }
+        }
+        return;
+    }
+
+    const int team = tid / team_size;
+    const int t = tid - team * team_size;
+    const int wpt = team_size >> 5;
+    const int team_bar = 2 + team;
     pdl_wait();
 
     // ---- prologue: this thread's 32 x values ------------------------------------------
@@ -168,8 +191,8 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
 #pragma unroll
         for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
         ss = warp_sum(ss);
-        if (lane == 0) wsum[tid >> 5] = ss;
-        __syncthreads();
+        if (lane == 0) wsum[warp] = ss;
+        named_bar(team_bar, team_size);
         float tot = 0.0f;
         for (int w = 0; w < wpt; ++w) tot += wsum[team * wpt + w];
         const float inv = 1.0f / sqrtf(tot / static_cast<float>(p.cols) + p.eps);
@@ -250,21 +273,21 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
     float best_v = -INFINITY;
     int best_i = (tid == 0) ? r_begin : 0x7fffffff;
 
-    // ---- stream rows --------------------------------------------------------------------
-    for (int ci = 0; ci < nchunks; ++ci) {
+    // ---- stream this team's chunks ------------------------------------------------------
+    int it = 0;
+    for (int ci = team; ci < nchunks; ci += teams, ++it) {
         const int s = ci % nst;
         const int row0 = r_begin + ci * R;
         const int nr = min(R, r_end - row0);
-        mbar_wait_bounded(&bar[s], static_cast<uint32_t>((ci / nst) & 1), p.err);
+        mbar_wait_bounded(&full[s], static_cast<uint32_t>((ci / nst) & 1), p.err);
         const uint8_t* sb = stages + s * stage_bytes;
-        // Branch-free over the team's rows (a clamped row index and a predicated result), so
-        // the compiler can overlap the shared loads and dp4a chains of all RPT rows.
+        // Branch-free over the chunk's rows (clamped row index, predicated result), so the
+        // shared loads and dp4a chains of all RPT rows overlap.
         uint4 wv[RPT];
         float sc[RPT], off[RPT];
 #pragma unroll
         for (int jj = 0; jj < RPT; ++jj) {
-            const int jc = min(team + jj * teams, nr - 1);
-            const uint8_t* row = sb + jc * p.row_stride;
+            const uint8_t* row = sb + min(jj, nr - 1) * p.row_stride;
             wv[jj] = ld_shared_v4(row + 16 * t);
             if constexpr (META == kMetaSym16) {
                 sc[jj] = __half2float(*reinterpret_cast<const __half*>(row + p.meta_offset + 2 * (t >> 1)));
@@ -300,32 +323,33 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
                 val = dot * (sc[jj] * down) + nan_or_zero;
             else
                 val = dot * (sc[jj] * down) + off[jj] * xsum + nan_or_zero;
-            part[jj] = (team + jj * teams < nr) ? val : 0.0f;
+            part[jj] = (jj < nr) ? val : 0.0f;
         }
         const float v = reduce_rows<RPT>(part, lane);
-        float* rbuf = red + (ci & 1) * (kMaxRowsPerChunk * 32);
+        float* rbuf = red + (it & 1) * (kMaxRowsPerChunk * 32);
         if ((lane & (32 / RPT - 1)) == 0) {
-            const int j = team + (lane / (32 / RPT)) * teams;
-            if (j < nr) rbuf[j * 32 + wit] = v;
+            const int j = lane / (32 / RPT);
+            if (j < nr) rbuf[j * 32 + warp] = v;
         }
-        __syncthreads();
-        if (tid == 0 && ci + nst < nchunks) issue(ci + nst);
+        named_bar(team_bar, team_size);
+        if (t == 0) mbar_arrive(&empty[s]);  // every thread of the team is done with stage s
 
-        // ---- epilogue for the rows of this chunk ------------------------------------------
+        // ---- epilogue for the rows of this chunk (the team's first warp) -------------------
+        const int w0 = team * wpt;
         if constexpr (EPI == kEpiSwiglu) {
-            if (tid < (nr >> 1)) {
+            if (t < (nr >> 1)) {
                 float g = 0.0f, u = 0.0f;
                 for (int w = 0; w < wpt; ++w) {
-                    g += rbuf[(2 * tid) * 32 + w];
-                    u += rbuf[(2 * tid + 1) * 32 + w];
+                    g += rbuf[(2 * t) * 32 + w0 + w];
+                    u += rbuf[(2 * t + 1) * 32 + w0 + w];
                 }
-                p.out[(row0 >> 1) + tid] = dsilu(g) * u;  // custom_model.cpp:1226-1230
+                p.out[(row0 >> 1) + t] = dsilu(g) * u;  // custom_model.cpp:1226-1230
             }
         } else {
-            if (tid < nr) {
+            if (t < nr) {
                 float y = 0.0f;
-                for (int w = 0; w < wpt; ++w) y += rbuf[tid * 32 + w];
-                const int r = row0 + tid;
+                for (int w = 0; w < wpt; ++w) y += rbuf[t * 32 + w0 + w];
+                const int r = row0 + t;
                 if constexpr (EPI == kEpiStore) {
                     p.out[r] = y;
                 } else if constexpr (EPI == kEpiResidual) {
@@ -355,28 +379,34 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
     if constexpr (EPI == kEpiArgmax) {
         // Block result (lowest index on ties, gemvW4A16ArgmaxNeon :309-336), then the last
         // block to finish merges all blocks and runs the optional decode-step head work.
-        __shared__ int s_last;
-        if (tid < 32) {
+        __shared__ int s_last, s_token;
+        __shared__ float s_v[32];
+        __shared__ int s_i[32];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-                argmax_merge(best_v, best_i, ov, oi);
-            }
-            if (tid == 0) {
-                p.part_val[blockIdx.x] = best_v;
-                p.part_idx[blockIdx.x] = best_i;
-                __threadfence();
-                const unsigned done = atomicAdd(p.counter, 1u);
-                s_last = (done == gridDim.x - 1) ? 1 : 0;
-            }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+            argmax_merge(best_v, best_i, ov, oi);
         }
-        __syncthreads();
+        if (lane == 0) {
+            s_v[warp] = best_v;
+            s_i[warp] = best_i;
+        }
+        named_bar(1, consumers);
+        if (tid == 0) {
+            for (int w = 1; w < (consumers >> 5); ++w) argmax_merge(best_v, best_i, s_v[w], s_i[w]);
+            p.part_val[blockIdx.x] = best_v;
+            p.part_idx[blockIdx.x] = best_i;
+            __threadfence();
+            const unsigned done = atomicAdd(p.counter, 1u);
+            s_last = (done == gridDim.x - 1) ? 1 : 0;
+        }
+        named_bar(1, consumers);
         if (s_last) {
             __threadfence();
             float bv = -INFINITY;
             int bi = 0x7fffffff;
-            for (int b = tid; b < static_cast<int>(gridDim.x); b += blockDim.x)
+            for (int b = tid; b < static_cast<int>(gridDim.x); b += consumers)
                 argmax_merge(bv, bi, __ldcg(p.part_val + b), __ldcg(p.part_idx + b));
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
@@ -384,16 +414,14 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
                 const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
                 argmax_merge(bv, bi, ov, oi);
             }
-            __shared__ float s_v[32];
-            __shared__ int s_i[32];
+            named_bar(1, consumers);  // s_v / s_i reuse
             if (lane == 0) {
-                s_v[tid >> 5] = bv;
-                s_i[tid >> 5] = bi;
+                s_v[warp] = bv;
+                s_i[warp] = bi;
             }
-            __syncthreads();
-            __shared__ int s_token;
+            named_bar(1, consumers);
             if (tid == 0) {
-                for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) argmax_merge(bv, bi, s_v[w], s_i[w]);
+                for (int w = 1; w < (consumers >> 5); ++w) argmax_merge(bv, bi, s_v[w], s_i[w]);
                 if (bi < 0 || bi >= p.rows) bi = 0;
                 s_token = bi;
                 if (p.token_out) *p.token_out = bi;
@@ -410,10 +438,10 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
                 }
                 *p.counter = 0u;  // re-arm for the next launch
             }
-            __syncthreads();
+            named_bar(1, consumers);
             if (p.emb) {  // loadEmbeddingRow, custom_model.cpp:569-608 (bf16 -> fp32)
                 const uint16_t* e = p.emb + static_cast<size_t>(s_token) * p.hidden;
-                for (int k = tid; k < p.hidden; k += blockDim.x) p.hidden_out[k] = bf16_to_f32(e[k]);
+                for (int k = tid; k < p.hidden; k += consumers) p.hidden_out[k] = bf16_to_f32(e[k]);
             }
         }
     }

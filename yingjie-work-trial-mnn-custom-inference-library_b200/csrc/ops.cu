@@ -260,21 +260,35 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // Merge the splits in parallel: (max, sum) of every (split, head) pair to shared memory,
+    // one rescale weight per pair, then thread d sums its dimension over the splits.
+    __shared__ float s_pm[kAttnSplits * kAttnMaxGroup], s_pl[kAttnSplits * kAttnMaxGroup];
+    __shared__ float s_M[kAttnMaxGroup], s_invL[kAttnMaxGroup];
     const float* base = p.part + static_cast<size_t>(kh * kAttnSplits) * group * (hd + 2);
-    for (int g = 0; g < group; ++g) {
+    if (tid < kAttnSplits * group) {
+        const float* ps = base + tid * (hd + 2);  // tid = split * group + g
+        s_pm[tid] = __ldcg(ps + hd);
+        s_pl[tid] = __ldcg(ps + hd + 1);
+    }
+    __syncthreads();
+    if (tid < group) {
         float M = -INFINITY;
-        for (int s = 0; s < kAttnSplits; ++s) M = fmaxf(M, __ldcg(base + (s * group + g) * (hd + 2) + hd));
-        float Ls = 0.0f, O = 0.0f;
-        for (int s = 0; s < kAttnSplits; ++s) {
-            const float* ps = base + (s * group + g) * (hd + 2);
-            const float w = expf(__ldcg(ps + hd) - M);
-            Ls += __ldcg(ps + hd + 1) * w;
-            O += __ldcg(ps + tid) * w;
-        }
+        for (int s2 = 0; s2 < kAttnSplits; ++s2) M = fmaxf(M, s_pm[s2 * group + tid]);
+        float Ls = 0.0f;
+        for (int s2 = 0; s2 < kAttnSplits; ++s2) Ls += s_pl[s2 * group + tid] * expf(s_pm[s2 * group + tid] - M);
+        s_M[tid] = M;
+        s_invL[tid] = Ls > 0.0f ? 1.0f / Ls : 0.0f;
+    }
+    __syncthreads();
+    if (tid < kAttnSplits * group) s_pm[tid] = expf(s_pm[tid] - s_M[tid % group]);
+    __syncthreads();
+    for (int g = 0; g < group; ++g) {
+        float O = 0.0f;
+#pragma unroll 8
+        for (int s2 = 0; s2 < kAttnSplits; ++s2) O += __ldcg(base + (s2 * group + g) * (hd + 2) + tid) * s_pm[s2 * group + g];
         const int qh = kh * group + g;
         const float gate = p.qkv[static_cast<size_t>(qh) * 2 * hd + hd + tid];
-        const float inv = Ls > 0.0f ? 1.0f / Ls : 0.0f;
-        p.out[qh * hd + tid] = (O * inv) * dsigmoid(gate);  // output gate, custom_model.cpp:944-946
+        p.out[qh * hd + tid] = (O * s_invL[g]) * dsigmoid(gate);  // output gate, custom_model.cpp:944-946
     }
     if (tid == 0) p.counters[kh] = 0u;
 }
