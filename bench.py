@@ -282,7 +282,8 @@ def main():
                                                                          args.prompt + args.warmup + args.steps],
                        "kv_dtype": "f16" if args.kv_fp16 else "f32", "parallelism": f"replicas{world}",
                        "l2": "inputs larger than L2 (4.3 GB of weights streamed per step)",
-                       "cuda_graphs": True, "pdl": True},
+                       "step_execution": "persistent cooperative kernel" if info.get("persistent_step_kernel")
+                       else "CUDA graph of per-op kernels with PDL"},
             "prefill_tok_s": round(prefill_tok_s, 2),
             "step_bytes": int(alg_step),
             "step_roofline_frac": round(alg_step / (ms_max / args.steps * 1e-3) / 1e9 / peak, 4),

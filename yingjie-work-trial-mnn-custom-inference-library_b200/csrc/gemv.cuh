@@ -112,6 +112,191 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// x of one thread (32 columns) as three signed 8-bit limbs of round(x * 2^S).
+struct XLimbs {
+    uint32_t le[4][3], lo[4][3];  // even / odd columns of word i, limb l
+    int acc_init[3];              // symmetric layout: -8 * sum of limbs (zero folded in)
+    float down;                   // 2^(-S-4)
+    float xsum;                   // sum of the 32 x values (affine layout offset term)
+    float nan_or_zero;            // NaN when x holds a non-finite value (propagates like fp32)
+};
+
+// Load this thread's 32 x values and apply the prologue. Inter-phase activations are read
+// with ld.global.cg (L2) so a persistent kernel never sees a stale L1 line.
+template <int PRO>
+__device__ __forceinline__ void gemv_load_x(const GemvParams& p, int t, int lane, int warp, int team, int wpt,
+                                            int team_bar, int team_size, float* wsum, float (&xv)[32]) {
+    const float4* src = reinterpret_cast<const float4*>(p.x + 32 * t);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 v = __ldcg(src + i);
+        xv[4 * i] = v.x;
+        xv[4 * i + 1] = v.y;
+        xv[4 * i + 2] = v.z;
+        xv[4 * i + 3] = v.w;
+    }
+    if constexpr (PRO == kProRms) {
+        // rmsnormReference (ref_rmsnorm.cpp:8-17): x * (1/sqrt(mean(x^2)+eps)) * w
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
+        ss = warp_sum(ss);
+        if (lane == 0) wsum[warp] = ss;
+        named_bar(team_bar, team_size);
+        float tot = 0.0f;
+        for (int w = 0; w < wpt; ++w) tot += wsum[team * wpt + w];
+        const float inv = 1.0f / sqrtf(tot / static_cast<float>(p.cols) + p.eps);
+        const float4* wn = reinterpret_cast<const float4*>(p.norm_w + 32 * t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 g = wn[i];
+            xv[4 * i] = xv[4 * i] * inv * g.x;
+            xv[4 * i + 1] = xv[4 * i + 1] * inv * g.y;
+            xv[4 * i + 2] = xv[4 * i + 2] * inv * g.z;
+            xv[4 * i + 3] = xv[4 * i + 3] * inv * g.w;
+        }
+        named_bar(team_bar, team_size);  // wsum may be reused by the next phase
+    } else if constexpr (PRO == kProGatedRms) {
+        // applyGatedHeadRms (custom_model.cpp:329-349): per head of head_dim columns,
+        // out = in * inv * w * silu(z); head_dim/32 consecutive lanes share one head.
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
+        const int tph = p.head_dim >> 5;
+        for (int o = 1; o < tph; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.head_dim) + p.eps);
+        const int c0 = 32 * t;
+        const int d0 = c0 % p.head_dim;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) xv[i] = xv[i] * inv * p.norm_w[d0 + i] * dsilu(__ldcg(p.gate_z + c0 + i));
+    }
+}
+
+template <int META>
+__device__ __forceinline__ void gemv_make_limbs(const float (&xv)[32], XLimbs& L) {
+    float amax = 0.0f, xsum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        amax = fmaxf(amax, fabsf(xv[i]));
+        xsum += xv[i];
+    }
+    const bool finite = isfinite(amax) && isfinite(xsum);
+    int ex = 0;
+    frexpf(amax, &ex);
+    const int S = max(-100, min(100, 22 - ex));
+    const float up = ldexpf(1.0f, S);
+    L.down = ldexpf(1.0f, -S - 4);  // undoes 2^S and the x16 of the high nibbles
+    L.xsum = xsum;
+    L.nan_or_zero = finite ? 0.0f : __int_as_float(0x7fc00000);
+    int zs[3] = {0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int l = 0; l < 3; ++l) {
+            L.le[i][l] = 0u;
+            L.lo[i][l] = 0u;
+        }
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+#pragma unroll
+            for (int odd = 0; odd < 2; ++odd) {
+                const float xf = finite ? xv[8 * i + 2 * b + odd] : 0.0f;
+                int m = __float2int_rn(xf * up);
+                const int l0 = static_cast<int>(static_cast<int8_t>(m & 0xff));
+                m = (m - l0) >> 8;
+                const int l1 = static_cast<int>(static_cast<int8_t>(m & 0xff));
+                const int l2 = (m - l1) >> 8;
+                const int limb[3] = {l0, l1, l2};
+#pragma unroll
+                for (int l = 0; l < 3; ++l) {
+                    const uint32_t byte = static_cast<uint32_t>(limb[l] & 0xff) << (8 * b);
+                    if (odd)
+                        L.lo[i][l] |= byte;
+                    else
+                        L.le[i][l] |= byte;
+                    zs[l] += limb[l];
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int l = 0; l < 3; ++l) L.acc_init[l] = (META == kMetaSym16) ? -8 * zs[l] : 0;
+}
+
+// Partial dot products of this thread's 32 columns for the first nr (<= RPT) rows of a
+// chunk in shared memory. Branch-free over rows (clamped index, predicated result) so the
+// shared loads and dp4a chains of all RPT rows overlap.
+template <int META, int RPT>
+__device__ __forceinline__ void gemv_chunk_partials(const uint8_t* sb, int row_stride, int meta_offset, int t,
+                                                    int nr, const XLimbs& L, float (&part)[RPT]) {
+    uint4 wv[RPT];
+    float sc[RPT], off[RPT];
+#pragma unroll
+    for (int jj = 0; jj < RPT; ++jj) {
+        const uint8_t* row = sb + min(jj, nr - 1) * row_stride;
+        wv[jj] = ld_shared_v4(row + 16 * t);
+        if constexpr (META == kMetaSym16) {
+            sc[jj] = __half2float(*reinterpret_cast<const __half*>(row + meta_offset + 2 * (t >> 1)));
+            off[jj] = 0.0f;
+        } else {
+            const float2 sbv = *reinterpret_cast<const float2*>(row + meta_offset + 8 * (t >> 1));
+            sc[jj] = sbv.x;
+            off[jj] = sbv.y;
+        }
+    }
+#pragma unroll
+    for (int jj = 0; jj < RPT; ++jj) {
+        const uint32_t ws[4] = {wv[jj].x, wv[jj].y, wv[jj].z, wv[jj].w};
+        int ae[3] = {L.acc_init[0], L.acc_init[1], L.acc_init[2]};
+        int ao[3] = {0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t lw = ws[i] & 0x0F0F0F0Fu;
+            const uint32_t hw = ws[i] & 0xF0F0F0F0u;
+#pragma unroll
+            for (int l = 0; l < 3; ++l) {
+                ae[l] = dp4a_us(lw, L.le[i][l], ae[l]);
+                ao[l] = dp4a_us(hw, L.lo[i][l], ao[l]);
+            }
+        }
+        const float d2 = static_cast<float>(ae[2] * 16 + ao[2]);
+        const float d1 = static_cast<float>(ae[1] * 16 + ao[1]);
+        const float d0 = static_cast<float>(ae[0] * 16 + ao[0]);
+        const float dot = d2 * 65536.0f + (d1 * 256.0f + d0);
+        float val;
+        if constexpr (META == kMetaSym16)
+            val = dot * (sc[jj] * L.down) + L.nan_or_zero;
+        else
+            val = dot * (sc[jj] * L.down) + off[jj] * L.xsum + L.nan_or_zero;
+        part[jj] = (jj < nr) ? val : 0.0f;
+    }
+}
+
+// Epilogue of one finished row (everything except argmax and the SwiGLU pair).
+template <int EPI>
+__device__ __forceinline__ void gemv_epilogue_row(const GemvParams& p, int r, float y) {
+    if constexpr (EPI == kEpiStore) {
+        p.out[r] = y;
+    } else if constexpr (EPI == kEpiResidual) {
+        p.out[r] = __ldcg(p.out + r) + y;  // addResidual, custom_model.cpp:294-299
+    } else if constexpr (EPI == kEpiConv) {
+        if (r < p.conv_channels) {
+            // causal conv + SiLU + state shift, custom_model.cpp:985-1006
+            const int h = p.conv_k - 1;
+            const float* cw = p.conv_w + static_cast<size_t>(r) * p.conv_k;
+            float* st = p.conv_state + static_cast<size_t>(r) * h;
+            float acc = 0.0f;
+            for (int k = 0; k < h; ++k) acc += st[k] * cw[k];
+            acc += y * cw[h];
+            p.out[r] = dsilu(acc);
+            for (int k = 0; k + 1 < h; ++k) st[k] = st[k + 1];
+            if (h > 0) st[h - 1] = y;
+        } else {
+            p.out2[r - p.conv_channels] = y;
+        }
+    }
+}
+
 // Block = `teams` consumer teams of K/32 threads + one producer warp (the last warp).
 // The producer streams this block's row chunks into a ring of shared-memory stages with
 // 1-D bulk copies (full[s] completes when a stage has landed, empty[s] when its team has
@@ -172,104 +357,12 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
     const int team_bar = 2 + team;
     pdl_wait();
 
-    // ---- prologue: this thread's 32 x values ------------------------------------------
-    float xv[32];
+    XLimbs L;
     {
-        const float4* src = reinterpret_cast<const float4*>(p.x + 32 * t);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 v = src[i];
-            xv[4 * i] = v.x;
-            xv[4 * i + 1] = v.y;
-            xv[4 * i + 2] = v.z;
-            xv[4 * i + 3] = v.w;
-        }
+        float xv[32];
+        gemv_load_x<PRO>(p, t, lane, warp, team, wpt, team_bar, team_size, wsum, xv);
+        gemv_make_limbs<META>(xv, L);
     }
-    if constexpr (PRO == kProRms) {
-        // rmsnormReference (ref_rmsnorm.cpp:8-17): x * (1/sqrt(mean(x^2)+eps)) * w
-        float ss = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
-        ss = warp_sum(ss);
-        if (lane == 0) wsum[warp] = ss;
-        named_bar(team_bar, team_size);
-        float tot = 0.0f;
-        for (int w = 0; w < wpt; ++w) tot += wsum[team * wpt + w];
-        const float inv = 1.0f / sqrtf(tot / static_cast<float>(p.cols) + p.eps);
-        const float4* wn = reinterpret_cast<const float4*>(p.norm_w + 32 * t);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 g = wn[i];
-            xv[4 * i] = xv[4 * i] * inv * g.x;
-            xv[4 * i + 1] = xv[4 * i + 1] * inv * g.y;
-            xv[4 * i + 2] = xv[4 * i + 2] * inv * g.z;
-            xv[4 * i + 3] = xv[4 * i + 3] * inv * g.w;
-        }
-    } else if constexpr (PRO == kProGatedRms) {
-        // applyGatedHeadRms (custom_model.cpp:329-349): per head of head_dim columns,
-        // out = in * inv * w * silu(z); head_dim/32 consecutive lanes share one head.
-        float ss = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
-        const int tph = p.head_dim >> 5;
-        for (int o = 1; o < tph; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.head_dim) + p.eps);
-        const int c0 = 32 * t;
-        const int d0 = c0 % p.head_dim;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) xv[i] = xv[i] * inv * p.norm_w[d0 + i] * dsilu(p.gate_z[c0 + i]);
-    }
-
-    // ---- x -> three signed 8-bit limbs of round(x * 2^S) ------------------------------
-    float amax = 0.0f, xsum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        amax = fmaxf(amax, fabsf(xv[i]));
-        xsum += xv[i];
-    }
-    const bool finite = isfinite(amax) && isfinite(xsum);
-    int ex = 0;
-    frexpf(amax, &ex);
-    const int S = max(-100, min(100, 22 - ex));
-    const float up = ldexpf(1.0f, S);
-    const float down = ldexpf(1.0f, -S - 4);  // undoes 2^S and the x16 of the high nibbles
-    uint32_t le[4][3], lo[4][3];
-    int zs[3] = {0, 0, 0};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-#pragma unroll
-        for (int l = 0; l < 3; ++l) {
-            le[i][l] = 0u;
-            lo[i][l] = 0u;
-        }
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-#pragma unroll
-            for (int odd = 0; odd < 2; ++odd) {
-                const float xf = finite ? xv[8 * i + 2 * b + odd] : 0.0f;
-                int m = __float2int_rn(xf * up);
-                const int l0 = static_cast<int>(static_cast<int8_t>(m & 0xff));
-                m = (m - l0) >> 8;
-                const int l1 = static_cast<int>(static_cast<int8_t>(m & 0xff));
-                const int l2 = (m - l1) >> 8;
-                const int limb[3] = {l0, l1, l2};
-#pragma unroll
-                for (int l = 0; l < 3; ++l) {
-                    const uint32_t byte = static_cast<uint32_t>(limb[l] & 0xff) << (8 * b);
-                    if (odd)
-                        lo[i][l] |= byte;
-                    else
-                        le[i][l] |= byte;
-                    zs[l] += limb[l];
-                }
-            }
-        }
-    }
-    int acc_init[3];
-#pragma unroll
-    for (int l = 0; l < 3; ++l) acc_init[l] = (META == kMetaSym16) ? -8 * zs[l] : 0;
-
-    const float nan_or_zero = finite ? 0.0f : __int_as_float(0x7fc00000);
     float best_v = -INFINITY;
     int best_i = (tid == 0) ? r_begin : 0x7fffffff;
 
@@ -280,51 +373,8 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
         const int row0 = r_begin + ci * R;
         const int nr = min(R, r_end - row0);
         mbar_wait_bounded(&full[s], static_cast<uint32_t>((ci / nst) & 1), p.err);
-        const uint8_t* sb = stages + s * stage_bytes;
-        // Branch-free over the chunk's rows (clamped row index, predicated result), so the
-        // shared loads and dp4a chains of all RPT rows overlap.
-        uint4 wv[RPT];
-        float sc[RPT], off[RPT];
-#pragma unroll
-        for (int jj = 0; jj < RPT; ++jj) {
-            const uint8_t* row = sb + min(jj, nr - 1) * p.row_stride;
-            wv[jj] = ld_shared_v4(row + 16 * t);
-            if constexpr (META == kMetaSym16) {
-                sc[jj] = __half2float(*reinterpret_cast<const __half*>(row + p.meta_offset + 2 * (t >> 1)));
-                off[jj] = 0.0f;
-            } else {
-                const float2 sbv = *reinterpret_cast<const float2*>(row + p.meta_offset + 8 * (t >> 1));
-                sc[jj] = sbv.x;
-                off[jj] = sbv.y;
-            }
-        }
         float part[RPT];
-#pragma unroll
-        for (int jj = 0; jj < RPT; ++jj) {
-            const uint32_t ws[4] = {wv[jj].x, wv[jj].y, wv[jj].z, wv[jj].w};
-            int ae[3] = {acc_init[0], acc_init[1], acc_init[2]};
-            int ao[3] = {0, 0, 0};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t lw = ws[i] & 0x0F0F0F0Fu;
-                const uint32_t hw = ws[i] & 0xF0F0F0F0u;
-#pragma unroll
-                for (int l = 0; l < 3; ++l) {
-                    ae[l] = dp4a_us(lw, le[i][l], ae[l]);
-                    ao[l] = dp4a_us(hw, lo[i][l], ao[l]);
-                }
-            }
-            const float d2 = static_cast<float>(ae[2] * 16 + ao[2]);
-            const float d1 = static_cast<float>(ae[1] * 16 + ao[1]);
-            const float d0 = static_cast<float>(ae[0] * 16 + ao[0]);
-            const float dot = d2 * 65536.0f + (d1 * 256.0f + d0);
-            float val;
-            if constexpr (META == kMetaSym16)
-                val = dot * (sc[jj] * down) + nan_or_zero;
-            else
-                val = dot * (sc[jj] * down) + off[jj] * xsum + nan_or_zero;
-            part[jj] = (jj < nr) ? val : 0.0f;
-        }
+        gemv_chunk_partials<META, RPT>(stages + s * stage_bytes, p.row_stride, p.meta_offset, t, nr, L, part);
         const float v = reduce_rows<RPT>(part, lane);
         float* rbuf = red + (it & 1) * (kMaxRowsPerChunk * 32);
         if ((lane & (32 / RPT - 1)) == 0) {
@@ -349,29 +399,10 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
             if (t < nr) {
                 float y = 0.0f;
                 for (int w = 0; w < wpt; ++w) y += rbuf[t * 32 + w0 + w];
-                const int r = row0 + t;
-                if constexpr (EPI == kEpiStore) {
-                    p.out[r] = y;
-                } else if constexpr (EPI == kEpiResidual) {
-                    p.out[r] += y;  // addResidual, custom_model.cpp:294-299
-                } else if constexpr (EPI == kEpiConv) {
-                    if (r < p.conv_channels) {
-                        // causal conv + SiLU + state shift, custom_model.cpp:985-1006
-                        const int h = p.conv_k - 1;
-                        const float* cw = p.conv_w + static_cast<size_t>(r) * p.conv_k;
-                        float* st = p.conv_state + static_cast<size_t>(r) * h;
-                        float acc = 0.0f;
-                        for (int k = 0; k < h; ++k) acc += st[k] * cw[k];
-                        acc += y * cw[h];
-                        p.out[r] = dsilu(acc);
-                        for (int k = 0; k + 1 < h; ++k) st[k] = st[k + 1];
-                        if (h > 0) st[h - 1] = y;
-                    } else {
-                        p.out2[r - p.conv_channels] = y;
-                    }
-                } else if constexpr (EPI == kEpiArgmax) {
-                    argmax_merge(best_v, best_i, y, r);
-                }
+                if constexpr (EPI == kEpiArgmax)
+                    argmax_merge(best_v, best_i, y, row0 + t);
+                else
+                    gemv_epilogue_row<EPI>(p, row0 + t, y);
             }
         }
     }

@@ -9,6 +9,7 @@
 #include <vector>
 
 #include "gemv.hpp"
+#include "stepper.cuh"
 
 namespace xqb {
 
@@ -48,6 +49,7 @@ struct Options {
     int device = 0;
     bool kv_fp16 = false;
     bool use_graphs = true;
+    bool persistent = true;  // one cooperative persistent kernel per step when the model allows it
     int initial_capacity = 8192;
 };
 
@@ -85,6 +87,7 @@ public:
     bool kv_fp16() const { return opts_.kv_fp16; }
     int kernels_per_decode_step() const;
     int kernels_per_prefill_step() const;
+    bool persistent() const { return persistent_; }
     cudaStream_t stream() const { return stream_; }
     const std::vector<DevLayer>& layers() const { return layers_; }
     const DevMatrix& lm_head() const { return lm_head_; }
@@ -103,6 +106,8 @@ private:
     bool capture_graphs(std::string* error);
     void destroy_graphs();
     bool run_step(bool decode, std::string* error);
+    bool build_phases(std::string* error);
+    bool persistent_eligible(int capacity) const;
     template <typename T>
     bool dev_alloc(T** p, size_t count, std::string* error);
     bool upload_vec(float** dst, const std::vector<float>& v, std::string* error);
@@ -139,6 +144,14 @@ private:
     size_t weight_bytes_ = 0, device_bytes_ = 0;
     std::vector<void*> allocs_;
     bool loaded_ = false;
+    // persistent step kernel
+    bool persistent_ = false;
+    int meta_kind_ = 0;
+    int step_slots_ = 0;
+    PhaseDesc* d_phases_decode_ = nullptr;
+    PhaseDesc* d_phases_prefill_ = nullptr;
+    int n_phases_ = 0;
+    unsigned* d_grid_bar_ = nullptr;
 };
 
 }  // namespace xqb

@@ -24,6 +24,16 @@ struct DeltaParams {
 // grid (nv, dv / kDeltaCols), block dk (= 128)
 __global__ void gated_delta_kernel(const DeltaParams p);
 
+// Shared scratch of one DeltaNet work item (one value head, kDeltaCols columns).
+struct DeltaScratch {
+    float red[4][kDeltaCols];
+    float bc[kDeltaCols];
+    float nrm[2][4];
+};
+// One DeltaNet work item run by 128 threads (i = key row) that synchronise with
+// bar.sync(bar_id, 128).
+// (defined in ops_device.cuh)
+
 // ---- Full attention ------------------------------------------------------------------
 constexpr int kAttnSplits = 32;   // blocks per kv head (split over positions)
 constexpr int kAttnThreads = 256;  // = head_dim
@@ -47,6 +57,18 @@ struct AttnParams {
     float* out;           // [nq*hd]
     unsigned* err;
 };
+
+// Shared scratch of one attention work item besides the dynamic [group][hd] q and
+// [group][cmax] score arrays.
+struct AttnScratch {
+    float m[kAttnMaxGroup], l[kAttnMaxGroup];
+    float pm[kAttnSplits * kAttnMaxGroup], pl[kAttnSplits * kAttnMaxGroup];
+    float M[kAttnMaxGroup], invL[kAttnMaxGroup];
+    int last;
+};
+// One attention work item (kv head kh, split) run by kAttnThreads threads synchronising with
+// bar.sync(bar_id, kAttnThreads); dyn = group*hd + group*cmax floats of shared memory.
+// (defined in ops_device.cuh)
 
 // Launch the attention kernel (fp16 or fp32 KV cache); grid (nkv, kAttnSplits).
 cudaError_t launch_attention(const AttnParams& p, bool kv_fp16, size_t smem, cudaStream_t s, bool pdl);

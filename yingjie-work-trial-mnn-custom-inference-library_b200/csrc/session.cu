@@ -351,7 +351,8 @@ public:
         if (model_)
           o << ",\"weight_bytes\":" << model_->weight_bytes() << ",\"device_bytes\":" << model_->device_bytes()
             << ",\"kv_capacity\":" << model_->capacity()
-            << ",\"kernels_per_decode_step\":" << model_->kernels_per_decode_step();
+            << ",\"kernels_per_decode_step\":" << model_->kernels_per_decode_step()
+            << ",\"persistent_step_kernel\":" << (model_->persistent() ? "true" : "false");
         o << ",\"selected_kernels\":\"" << json_escape(coverage()) << "\"}";
         return copy_json(o.str(), buf, cap);
     }
@@ -440,7 +441,7 @@ private:
           << "rmsnorm=fused_gemv_prologue;rope=fused_attention;attention=split_k_flash_decode_"
           << (cuda_.kv_fp16 ? "kv_f16" : "kv_f32") << ";linear_attention_state=gated_delta_column_split;"
           << "linear_attention_conv=fused_gemv_epilogue;sampling=device_greedy_argmax;"
-          << "prefill_kv_build=token_serial_cuda_graph;cuda_graphs=" << (cuda_.use_graphs ? "on" : "off")
+          << "prefill_kv_build=token_serial;step=" << (model_ && model_->persistent() ? "persistent_kernel" : "cuda_graph")
           << ";fallback_ops=none";
         return o.str();
     }
