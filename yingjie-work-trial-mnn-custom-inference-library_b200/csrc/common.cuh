@@ -31,9 +31,12 @@ enum DeviceError : unsigned {
     kErrBadShape = 2u,        // a kernel saw a configuration it does not support
 };
 
-// Every spin-wait in these kernels is bounded by this many polls (~seconds), after which
-// the kernel records kErrBarrierTimeout and returns instead of hanging the GPU.
-constexpr uint32_t kSpinLimit = 1u << 26;
+// Every spin-wait in these kernels is bounded in time: after kWaitLimitNs it records
+// kErrBarrierTimeout in the error word and gives up, and every later wait in any block
+// returns at once when it sees that bit, so a kernel that cannot make progress ends within
+// seconds instead of hanging the GPU.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint32_t kSpinLimit = 1u << 30;         // poll cap on top of the time limit
 
 // ------------------------------------------------------------------------------------
 // PTX wrappers
@@ -80,12 +83,43 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait; false (and the error bit set) if the budget ran out.
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Slow path of every bounded wait: true while the caller may keep waiting.
+__device__ __forceinline__ bool wait_budget_left(uint64_t t0, uint32_t i, unsigned* err) {
+    if ((i & 255u) != 0u) return i < kSpinLimit;
+    if (err && (*reinterpret_cast<volatile unsigned*>(err) & kErrBarrierTimeout)) return false;
+    if (global_ns() - t0 > kWaitLimitNs || i >= kSpinLimit) {
+        if (err) atomicOr(err, kErrBarrierTimeout);
+        return false;
+    }
+    return true;
+}
+
+// Bounded mbarrier wait; false (and the error bit set) if it gave up.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, unsigned* err) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-    if (err) atomicOr(err, kErrBarrierTimeout);
-    return false;
+        if (!wait_budget_left(t0, i, err)) return false;
+    }
+}
+
+// Wait for copies this block issued before it exits (after an error as well): bounded by
+// its own deadline, independent of the error bit.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, parity))
+        if (global_ns() - t0 > kWaitLimitNs) return;
+}
+
+__device__ __forceinline__ bool error_raised(const unsigned* err) {
+    return err && (*reinterpret_cast<const volatile unsigned*>(err) & kErrBarrierTimeout);
 }
 
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {

@@ -339,14 +339,21 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
     if (warp == (consumers >> 5)) {
         // Producer: weights never depend on the previous kernel, so no griddepcontrol.wait.
         if (lane == 0) {
+            int issued = 0;
             for (int ci = 0; ci < nchunks; ++ci) {
                 const int s = ci % nst;
-                if (ci >= nst) mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((ci / nst) - 1) & 1), p.err);
+                if (ci >= nst && !mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((ci / nst) - 1) & 1), p.err))
+                    break;
+                if (error_raised(p.err)) break;
                 const int row0 = r_begin + ci * R;
                 const uint32_t bytes = static_cast<uint32_t>(min(R, r_end - row0) * p.row_stride);
                 mbar_expect_tx(&full[s], bytes);
                 bulk_g2s(stages + s * stage_bytes, p.w + static_cast<size_t>(row0) * p.row_stride, bytes, &full[s]);
+                ++issued;
             }
+            // Every issued copy has landed before this block can exit.
+            for (int k = max(0, issued - nst); k < issued; ++k)
+                mbar_wait_drain(&full[k % nst], static_cast<uint32_t>((k / nst) & 1));
         }
         return;
     }

@@ -232,23 +232,35 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         // Producer: stream this block's rows of every GEMV phase, in phase order.
         if (c.lane == 0) {
             int g = 0;
-            for (int ph = 0; ph < P.nphases; ++ph) {
+            bool stop = false;
+            for (int ph = 0; ph < P.nphases && !stop; ++ph) {
                 const PhaseDesc& D = P.phases[ph];
                 if (D.kind != kPhaseGemv) continue;
                 int r_begin, r_end, nchunks;
                 block_rows(D.g, &r_begin, &r_end, &nchunks);
-                for (int ci = 0; ci < nchunks; ++ci, ++g) {
+                for (int ci = 0; ci < nchunks; ++ci) {
                     const int s = g % c.nslots;
-                    if (g >= c.nslots)
-                        mbar_wait_bounded(&c.empty[s], static_cast<uint32_t>(((g / c.nslots) - 1) & 1), P.err);
+                    if (g >= c.nslots &&
+                        !mbar_wait_bounded(&c.empty[s], static_cast<uint32_t>(((g / c.nslots) - 1) & 1), P.err)) {
+                        stop = true;
+                        break;
+                    }
+                    if (error_raised(P.err)) {
+                        stop = true;
+                        break;
+                    }
                     const int row0 = r_begin + ci * D.g.rows_per_chunk;
                     const uint32_t bytes =
                         static_cast<uint32_t>(min(D.g.rows_per_chunk, r_end - row0) * D.g.row_stride);
                     mbar_expect_tx(&c.full[s], bytes);
                     bulk_g2s(c.ring + static_cast<size_t>(s) * kStepSlotBytes,
                              D.g.w + static_cast<size_t>(row0) * D.g.row_stride, bytes, &c.full[s]);
+                    ++g;
                 }
             }
+            // Every issued copy has landed before this block can exit.
+            for (int k = max(0, g - c.nslots); k < g; ++k)
+                mbar_wait_drain(&c.full[k % c.nslots], static_cast<uint32_t>((k / c.nslots) & 1));
         }
         return;
     }
@@ -261,12 +273,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         if (ph > 0) {  // every phase consumes the previous phase's output
             if (c.tid == 0) {
                 const unsigned target = static_cast<unsigned>(ph) * G;
-                uint32_t n = 0;
-                while (ld_acquire(P.grid_bar) < target) {
-                    if (++n >= kSpinLimit) {
-                        atomicOr(P.err, kErrBarrierTimeout);
-                        break;
-                    }
+                if (ld_acquire(P.grid_bar) < target) {
+                    const uint64_t t0 = global_ns();
+                    for (uint32_t n = 1; ld_acquire(P.grid_bar) < target; ++n)
+                        if (!wait_budget_left(t0, n, P.err)) break;
                 }
             }
             named_bar(1, kStepConsumers);
