@@ -4,6 +4,8 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <array>
+#include <map>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -370,6 +372,9 @@ bool DeviceModel::load(const std::string& dir, const Options& opts, std::string*
         if (persistent_) {
             step_slots_ = step_max_slots();
             if (!build_phases(error)) return false;
+            const char* tr = std::getenv("XQ_STEP_TRACE");
+            if (tr && std::atoi(tr) != 0 && !dev_alloc(&d_step_trace_, 3 * static_cast<size_t>(n_phases_), error))
+                return false;
         }
     }
     if (cudaDeviceSynchronize() != cudaSuccess) {
@@ -576,6 +581,22 @@ bool DeviceModel::build_phases(std::string* error) {
     dec.insert(dec.end(), forward.begin(), forward.end());
     pre.insert(pre.end(), forward.begin(), forward.end());
     n_phases_ = static_cast<int>(dec.size());
+    phase_names_.clear();
+    for (const PhaseDesc& D : dec) {
+        std::string n;
+        if (D.kind == kPhaseDelta) n = "delta";
+        else if (D.kind == kPhaseAttn) n = "attention";
+        else if (D.kind == kPhaseEmbed) n = "embed";
+        else if (D.epi == kEpiArgmax) n = "lm_head_argmax";
+        else if (D.epi == kEpiConv) n = "gemv_in_proj_conv";
+        else if (D.epi == kEpiSwiglu) n = "gemv_gate_up";
+        else if (D.pro == kProGatedRms) n = "gemv_out_proj";
+        else if (D.epi == kEpiStore) n = "gemv_qkv";
+        else if (D.g.cols == d.inter) n = "gemv_down";
+        else n = "gemv_o_proj";
+        phase_names_.push_back(n);
+    }
+    phase_ns_.assign(3 * static_cast<size_t>(n_phases_), 0.0);
     for (int which = 0; which < 2; ++which) {
         PhaseDesc*& dst = which == 0 ? d_phases_decode_ : d_phases_prefill_;
         const std::vector<PhaseDesc>& src = which == 0 ? dec : pre;
@@ -786,7 +807,21 @@ bool DeviceModel::run_step(bool decode, std::string* error) {
         sp.vocab = d_.vocab;
         sp.pos = d_pos_;
         sp.next_pos = d_next_pos_;
+        sp.trace = decode ? d_step_trace_ : nullptr;
         const cudaError_t e = launch_decode_step(sp, meta_kind_, opts_.kv_fp16, num_sms_, stream_);
+        if (e == cudaSuccess && sp.trace) {
+            std::vector<unsigned long long> t(3 * static_cast<size_t>(n_phases_));
+            cudaMemcpyAsync(t.data(), d_step_trace_, t.size() * 8, cudaMemcpyDeviceToHost, stream_);
+            cudaStreamSynchronize(stream_);
+            for (int ph = 0; ph < n_phases_; ++ph) {
+                const double start = static_cast<double>(t[3 * ph]);
+                const double prev_end = ph ? static_cast<double>(t[3 * (ph - 1) + 2]) : start;
+                phase_ns_[3 * ph] += start - prev_end;                                        // barrier latency
+                phase_ns_[3 * ph + 1] += static_cast<double>(t[3 * ph + 1]) - start;          // block 0 work
+                phase_ns_[3 * ph + 2] += static_cast<double>(t[3 * ph + 2]) - start;          // until last arrival
+            }
+            ++traced_steps_;
+        }
         if (e != cudaSuccess) {
             *error = std::string("step kernel launch failed: ") + cudaGetErrorString(e);
             return false;
@@ -978,6 +1013,28 @@ bool DeviceModel::logits(std::vector<float>* out, std::string* error) {
         return false;
     }
     return true;
+}
+
+std::string DeviceModel::phase_trace_summary() const {
+    if (!traced_steps_) return "";
+    std::map<std::string, std::array<double, 4>> agg;
+    for (int ph = 0; ph < n_phases_; ++ph) {
+        auto& a = agg[phase_names_[ph]];
+        a[0] += 1;
+        for (int k = 0; k < 3; ++k) a[k + 1] += phase_ns_[3 * ph + k] / traced_steps_;
+    }
+    std::ostringstream o;
+    o << "{\"steps\":" << traced_steps_ << ",\"phases\":[";
+    bool first = true;
+    for (const auto& kv : agg) {
+        if (!first) o << ",";
+        first = false;
+        o << "{\"name\":\"" << kv.first << "\",\"count\":" << kv.second[0] << ",\"barrier_us\":"
+          << kv.second[1] / 1000.0 << ",\"block0_us\":" << kv.second[2] / 1000.0 << ",\"last_arrival_us\":"
+          << kv.second[3] / 1000.0 << "}";
+    }
+    o << "]}";
+    return o.str();
 }
 
 unsigned DeviceModel::device_errors() {

@@ -152,6 +152,16 @@ private:
     PhaseDesc* d_phases_prefill_ = nullptr;
     int n_phases_ = 0;
     unsigned* d_grid_bar_ = nullptr;
+    unsigned long long* d_step_trace_ = nullptr;  // XQ_STEP_TRACE=1: per-phase timestamps
+    std::vector<double> phase_ns_;                // accumulated [phase][3] durations
+    std::vector<std::string> phase_names_;
+    int traced_steps_ = 0;
+
+public:
+    // Per-phase device time summary of the persistent kernel (empty unless tracing).
+    std::string phase_trace_summary() const;
+
+private:
 };
 
 }  // namespace xqb

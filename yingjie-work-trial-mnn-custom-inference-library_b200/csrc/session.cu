@@ -353,6 +353,8 @@ public:
             << ",\"kv_capacity\":" << model_->capacity()
             << ",\"kernels_per_decode_step\":" << model_->kernels_per_decode_step()
             << ",\"persistent_step_kernel\":" << (model_->persistent() ? "true" : "false");
+        if (model_ && !model_->phase_trace_summary().empty())
+            o << ",\"step_phase_trace\":" << model_->phase_trace_summary();
         o << ",\"selected_kernels\":\"" << json_escape(coverage()) << "\"}";
         return copy_json(o.str(), buf, cap);
     }

@@ -281,6 +281,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             }
             named_bar(1, kStepConsumers);
         }
+        if (P.trace && blockIdx.x == 0 && c.tid == 0) P.trace[3 * ph] = global_ns();
         if (D.kind == kPhaseGemv) {
             gemv_dispatch<META>(D, c);
         } else if (D.kind == kPhaseDelta) {
@@ -313,8 +314,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         }
         named_bar(1, kStepConsumers);
         if (c.tid == 0) {
+            if (P.trace && blockIdx.x == 0) P.trace[3 * ph + 1] = global_ns();
             __threadfence();
             const unsigned old = atomicAdd(P.grid_bar, 1u);
+            if (P.trace && old == static_cast<unsigned>(ph + 1) * G - 1) P.trace[3 * ph + 2] = global_ns();
             if (ph == P.nphases - 1 && old == static_cast<unsigned>(P.nphases) * G - 1)
                 atomicExch(P.grid_bar, 0u);  // everybody has arrived; nobody waits any more
         }

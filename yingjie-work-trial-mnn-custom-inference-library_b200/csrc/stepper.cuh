@@ -46,6 +46,9 @@ struct StepParams {
     int vocab;
     int* pos;
     int* next_pos;
+    // Optional per-phase device timestamps of block 0 ([nphases][3] ns: barrier passed, work
+    // done, and — for the last block to arrive — the arrival time) when non-null.
+    unsigned long long* trace;
 };
 
 // Launch one step (cooperative). kv_fp16 selects the KV-cache element type; meta_kind the
