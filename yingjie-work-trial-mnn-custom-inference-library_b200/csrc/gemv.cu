@@ -202,6 +202,7 @@ struct Tuning {
     int block = kTargetBlock;
     int rpt = 8;
     int blocks_per_sm = 2;
+    int evict_first = 1;
     int ring_bytes = kRingBudgetBytes;
 };
 
@@ -211,12 +212,19 @@ const Tuning& tuning() {
         if (const char* e = std::getenv("XQ_GEMV_BLOCK")) v.block = std::max(32, std::min(kMaxBlock, std::atoi(e)));
         if (const char* e = std::getenv("XQ_GEMV_RPT")) v.rpt = std::atoi(e) >= 8 ? 8 : 4;
         if (const char* e = std::getenv("XQ_GEMV_BPS")) v.blocks_per_sm = std::max(1, std::min(4, std::atoi(e)));
+        if (const char* e = std::getenv("XQ_L2_EVICT_FIRST")) v.evict_first = std::atoi(e) != 0;
         if (const char* e = std::getenv("XQ_GEMV_RING_KB"))
             v.ring_bytes = std::max(16, std::min(200, std::atoi(e))) * 1024;
         return v;
     }();
     return t;
 }
+
+}  // namespace
+
+int gemv_evict_first() { return tuning().evict_first; }
+
+namespace {
 
 Shape shape_for(const DevMatrix& m) {
     const Tuning& tu = tuning();
@@ -296,6 +304,7 @@ bool launch_gemv(const DevMatrix& m, int pro, int epi, GemvParams p, int unit, c
     p.rows_per_chunk = s.rows_per_chunk;
     p.stages = s.stages;
     p.unit = unit;
+    p.evict_first = tuning().evict_first;
     const dim3 grid(gemv_grid(m, unit, ctx.num_sms, max_blocks));
     cudaError_t e = cudaErrorInvalidValue;
 #define XQB_CASE(PRO, EPI)                                                          \

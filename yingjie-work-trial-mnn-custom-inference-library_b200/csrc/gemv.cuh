@@ -43,6 +43,7 @@ struct GemvParams {
     int rows_per_chunk;  // R, even
     int stages;          // depth of the shared-memory ring, <= kMaxStages
     int unit;            // CTA row ranges are multiples of this (2 for gate/up pairs)
+    int evict_first;     // stream the rows with the L2 evict-first policy
     // prologue
     const float* x;
     const float* norm_w;  // kProRms: [cols]; kProGatedRms: [head_dim]
@@ -126,14 +127,29 @@ struct XLimbs {
 template <int PRO>
 __device__ __forceinline__ void gemv_load_x(const GemvParams& p, int t, int lane, int warp, int team, int wpt,
                                             int team_bar, int team_size, float* wsum, float (&xv)[32]) {
+    // Every global load of the prologue is issued before the first use: under a saturated
+    // memory system each dependent round trip costs microseconds.
     const float4* src = reinterpret_cast<const float4*>(p.x + 32 * t);
+    float4 a[8], b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = __ldcg(src + i);
+    if constexpr (PRO == kProRms) {
+        const float4* wn = reinterpret_cast<const float4*>(p.norm_w + 32 * t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) b[i] = __ldg(wn + i);
+    }
+    float4 z[8];
+    if constexpr (PRO == kProGatedRms) {
+        const float4* gz = reinterpret_cast<const float4*>(p.gate_z + 32 * t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) z[i] = __ldcg(gz + i);
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float4 v = __ldcg(src + i);
-        xv[4 * i] = v.x;
-        xv[4 * i + 1] = v.y;
-        xv[4 * i + 2] = v.z;
-        xv[4 * i + 3] = v.w;
+        xv[4 * i] = a[i].x;
+        xv[4 * i + 1] = a[i].y;
+        xv[4 * i + 2] = a[i].z;
+        xv[4 * i + 3] = a[i].w;
     }
     if constexpr (PRO == kProRms) {
         // rmsnormReference (ref_rmsnorm.cpp:8-17): x * (1/sqrt(mean(x^2)+eps)) * w
@@ -146,7 +162,64 @@ __device__ __forceinline__ void gemv_load_x(const GemvParams& p, int t, int lane
         float tot = 0.0f;
         for (int w = 0; w < wpt; ++w) tot += wsum[team * wpt + w];
         const float inv = 1.0f / sqrtf(tot / static_cast<float>(p.cols) + p.eps);
-        const float4* wn = reinterpret_cast<const float4*>(p.norm_w + 32 * t);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            xv[4 * i] = xv[4 * i] * inv * b[i].x;
+            xv[4 * i + 1] = xv[4 * i + 1] * inv * b[i].y;
+            xv[4 * i + 2] = xv[4 * i + 2] * inv * b[i].z;
+            xv[4 * i + 3] = xv[4 * i + 3] * inv * b[i].w;
+        }
+        named_bar(team_bar, team_size);  // wsum may be reused by the next phase
+    } else if constexpr (PRO == kProGatedRms) {
+        // applyGatedHeadRms (custom_model.cpp:329-349): per head of head_dim columns,
+        // out = in * inv * w * silu(z); head_dim/32 consecutive lanes share one head.
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
+        const int tph = p.head_dim >> 5;
+        for (int o = 1; o < tph; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.head_dim) + p.eps);
+        // norm_w has head_dim entries shared by every head: an L1 hit for all but one warp.
+        const float4* wn = reinterpret_cast<const float4*>(p.norm_w + (32 * t) % p.head_dim);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            b[i] = __ldg(wn + i);
+            xv[4 * i] = xv[4 * i] * inv * b[i].x * dsilu(z[i].x);
+            xv[4 * i + 1] = xv[4 * i + 1] * inv * b[i].y * dsilu(z[i].y);
+            xv[4 * i + 2] = xv[4 * i + 2] * inv * b[i].z * dsilu(z[i].z);
+            xv[4 * i + 3] = xv[4 * i + 3] * inv * b[i].w * dsilu(z[i].w);
+        }
+    }
+}
+
+// Prologue from shared memory: the block's copy of x (and, for kProRms, norm_w [cols]; for
+// kProGatedRms, gate_z [cols] followed by norm_w [head_dim]) was brought in by bulk copies.
+// Same arithmetic, in the same order, as gemv_load_x.
+template <int PRO>
+__device__ __forceinline__ void gemv_x_from_smem(const GemvParams& p, const float* xs, const float* vs, int t,
+                                                 int lane, int warp, int team, int wpt, int team_bar, int team_size,
+                                                 float* wsum, float (&xv)[32]) {
+    const float4* src = reinterpret_cast<const float4*>(xs + 32 * t);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 a = src[i];
+        xv[4 * i] = a.x;
+        xv[4 * i + 1] = a.y;
+        xv[4 * i + 2] = a.z;
+        xv[4 * i + 3] = a.w;
+    }
+    if constexpr (PRO == kProRms) {
+        // rmsnormReference (ref_rmsnorm.cpp:8-17): x * (1/sqrt(mean(x^2)+eps)) * w
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
+        ss = warp_sum(ss);
+        if (lane == 0) wsum[warp] = ss;
+        named_bar(team_bar, team_size);
+        float tot = 0.0f;
+        for (int w = 0; w < wpt; ++w) tot += wsum[team * wpt + w];
+        const float inv = 1.0f / sqrtf(tot / static_cast<float>(p.cols) + p.eps);
+        const float4* wn = reinterpret_cast<const float4*>(vs + 32 * t);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const float4 g = wn[i];
@@ -165,10 +238,16 @@ __device__ __forceinline__ void gemv_load_x(const GemvParams& p, int t, int lane
         const int tph = p.head_dim >> 5;
         for (int o = 1; o < tph; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.head_dim) + p.eps);
-        const int c0 = 32 * t;
-        const int d0 = c0 % p.head_dim;
+        const float4* gz = reinterpret_cast<const float4*>(vs + 32 * t);
+        const float4* wn = reinterpret_cast<const float4*>(vs + p.cols + (32 * t) % p.head_dim);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) xv[i] = xv[i] * inv * p.norm_w[d0 + i] * dsilu(__ldcg(p.gate_z + c0 + i));
+        for (int i = 0; i < 8; ++i) {
+            const float4 z = gz[i], g = wn[i];
+            xv[4 * i] = xv[4 * i] * inv * g.x * dsilu(z.x);
+            xv[4 * i + 1] = xv[4 * i + 1] * inv * g.y * dsilu(z.y);
+            xv[4 * i + 2] = xv[4 * i + 2] * inv * g.z * dsilu(z.z);
+            xv[4 * i + 3] = xv[4 * i + 3] * inv * g.w * dsilu(z.w);
+        }
     }
 }
 
@@ -181,41 +260,50 @@ __device__ __forceinline__ void gemv_make_limbs(const float (&xv)[32], XLimbs& L
         xsum += xv[i];
     }
     const bool finite = isfinite(amax) && isfinite(xsum);
-    int ex = 0;
-    frexpf(amax, &ex);
+    // Block exponent: amax = f * 2^ex with f in [0.5, 1) (frexpf) for normal amax. A zero or
+    // subnormal amax takes the clamp S = 100; every scaled value then rounds to the same
+    // integer as with frexpf's exponent (zero stays zero, subnormals already clamp).
+    const int ex = ((__float_as_int(amax) >> 23) & 0xff) - 126;
     const int S = max(-100, min(100, 22 - ex));
-    const float up = ldexpf(1.0f, S);
-    L.down = ldexpf(1.0f, -S - 4);  // undoes 2^S and the x16 of the high nibbles
+    const float up = __int_as_float((S + 127) << 23);       // 2^S
+    L.down = __int_as_float((127 - S - 4) << 23);           // 2^(-S-4): undoes 2^S and the x16 of the high nibbles
     L.xsum = xsum;
     L.nan_or_zero = finite ? 0.0f : __int_as_float(0x7fc00000);
+    // m = round_to_nearest_even(x * 2^S), |m| < 2^22, as the low mantissa bits of
+    // x * 2^S + 1.5 * 2^23 (one rounding, in the fma). Its signed base-256 digits
+    // (d0 + 256 d1 + 65536 d2, each in [-128, 127]) are the bytes of m + 0x808080 with the top
+    // bit of each byte flipped. A non-finite x gives garbage digits; the NaN term replaces the
+    // row result then.
+    uint32_t u[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        u[i] = static_cast<uint32_t>(__float_as_int(fmaf(xv[i], up, 12582912.0f))) + (0x808080u - 0x4B400000u);
     int zs[3] = {0, 0, 0};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
 #pragma unroll
-        for (int l = 0; l < 3; ++l) {
-            L.le[i][l] = 0u;
-            L.lo[i][l] = 0u;
-        }
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-#pragma unroll
-            for (int odd = 0; odd < 2; ++odd) {
-                const float xf = finite ? xv[8 * i + 2 * b + odd] : 0.0f;
-                int m = __float2int_rn(xf * up);
-                const int l0 = static_cast<int>(static_cast<int8_t>(m & 0xff));
-                m = (m - l0) >> 8;
-                const int l1 = static_cast<int>(static_cast<int8_t>(m & 0xff));
-                const int l2 = (m - l1) >> 8;
-                const int limb[3] = {l0, l1, l2};
-#pragma unroll
-                for (int l = 0; l < 3; ++l) {
-                    const uint32_t byte = static_cast<uint32_t>(limb[l] & 0xff) << (8 * b);
-                    if (odd)
-                        L.lo[i][l] |= byte;
-                    else
-                        L.le[i][l] |= byte;
-                    zs[l] += limb[l];
-                }
+        for (int odd = 0; odd < 2; ++odd) {
+            // columns 8i + odd + {0, 2, 4, 6} -> bytes 0..3 of each limb word
+            const uint32_t a = u[8 * i + odd], b = u[8 * i + 2 + odd], cc = u[8 * i + 4 + odd],
+                           d = u[8 * i + 6 + odd];
+            const uint32_t ab01 = __byte_perm(a, b, 0x5140), cd01 = __byte_perm(cc, d, 0x5140);
+            const uint32_t ab2 = __byte_perm(a, b, 0x0062), cd2 = __byte_perm(cc, d, 0x0062);
+            const uint32_t w0 = __byte_perm(ab01, cd01, 0x5410) ^ 0x80808080u;
+            const uint32_t w1 = __byte_perm(ab01, cd01, 0x7632) ^ 0x80808080u;
+            const uint32_t w2 = __byte_perm(ab2, cd2, 0x5410) ^ 0x80808080u;
+            if (odd) {
+                L.lo[i][0] = w0;
+                L.lo[i][1] = w1;
+                L.lo[i][2] = w2;
+            } else {
+                L.le[i][0] = w0;
+                L.le[i][1] = w1;
+                L.le[i][2] = w2;
+            }
+            if constexpr (META == kMetaSym16) {
+                zs[0] = __dp4a(static_cast<int>(w0), 0x01010101, zs[0]);
+                zs[1] = __dp4a(static_cast<int>(w1), 0x01010101, zs[1]);
+                zs[2] = __dp4a(static_cast<int>(w2), 0x01010101, zs[2]);
             }
         }
     }
@@ -339,6 +427,7 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
     if (warp == (consumers >> 5)) {
         // Producer: weights never depend on the previous kernel, so no griddepcontrol.wait.
         if (lane == 0) {
+            const uint64_t pol = l2_evict_first_policy();
             int issued = 0;
             for (int ci = 0; ci < nchunks; ++ci) {
                 const int s = ci % nst;
@@ -347,7 +436,12 @@ __global__ void __launch_bounds__(kMaxBlock, 1) gemv_w4a16_kernel(const GemvPara
                 const int row0 = r_begin + ci * R;
                 const uint32_t bytes = static_cast<uint32_t>(min(R, r_end - row0) * p.row_stride);
                 mbar_expect_tx(&full[s], bytes);
-                bulk_g2s(stages + s * stage_bytes, p.w + static_cast<size_t>(row0) * p.row_stride, bytes, &full[s]);
+                if (p.evict_first)
+                    bulk_g2s_hint(stages + s * stage_bytes, p.w + static_cast<size_t>(row0) * p.row_stride, bytes,
+                                  &full[s], pol);
+                else
+                    bulk_g2s(stages + s * stage_bytes, p.w + static_cast<size_t>(row0) * p.row_stride, bytes,
+                             &full[s]);
                 ++issued;
             }
             // Every issued copy has landed before this block can exit.

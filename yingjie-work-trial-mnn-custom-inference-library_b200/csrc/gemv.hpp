@@ -52,6 +52,8 @@ struct LaunchCtx {
 };
 
 // Fill the shape fields of p from m and launch the fused kernel. unit: 2 for gate/up pairs.
+// Whether weight rows are streamed with the L2 evict-first policy (XQ_L2_EVICT_FIRST, default 1).
+int gemv_evict_first();
 bool launch_gemv(const DevMatrix& m, int pro, int epi, GemvParams p, int unit, const LaunchCtx& ctx,
                  int max_blocks = 0);
 // Number of blocks launch_gemv uses (argmax partial buffers are sized with this).

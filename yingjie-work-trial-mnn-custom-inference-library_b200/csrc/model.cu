@@ -143,6 +143,7 @@ DeviceModel::~DeviceModel() {
     free_matrix(&lm_head_);
     cudaFree(d_rope_);
     cudaFree(d_phases_decode_);
+    cudaFree(d_tmaps_);
     cudaFree(d_phases_prefill_);
     for (void* p : allocs_) cudaFree(p);
     if (h_token_) cudaFreeHost(h_token_);
@@ -371,9 +372,13 @@ bool DeviceModel::load(const std::string& dir, const Options& opts, std::string*
         persistent_ = want && persistent_eligible(capacity_) && step_init_device() == cudaSuccess;
         if (persistent_) {
             step_slots_ = step_max_slots();
+            step_inflight_ = step_slots_;
+            if (const char* v = std::getenv("XQ_STEP_INFLIGHT")) step_inflight_ = std::atoi(v);
+            step_inflight_ = std::max(1, std::min(step_inflight_, step_slots_));
+            if (const char* v = std::getenv("XQ_STEP_L2_PREFETCH")) step_l2_prefetch_ = std::atoi(v) != 0;
             if (!build_phases(error)) return false;
             const char* tr = std::getenv("XQ_STEP_TRACE");
-            if (tr && std::atoi(tr) != 0 && !dev_alloc(&d_step_trace_, 3 * static_cast<size_t>(n_phases_), error))
+            if (tr && std::atoi(tr) != 0 && !dev_alloc(&d_step_trace_, kStepTraceSlots * static_cast<size_t>(n_phases_), error))
                 return false;
         }
     }
@@ -465,7 +470,13 @@ bool DeviceModel::persistent_eligible(int capacity) const {
 // embedding (decode) or the prompt's embedding (prefill).
 bool DeviceModel::build_phases(std::string* error) {
     const ModelDims& d = d_;
+    bool staged_ok = true;  // every GEMV's inputs fit the step kernel's staging areas, 16-byte aligned
+    auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
     auto gemv = [&](const DevMatrix& m, int pro, int epi, int unit, GemvParams g) {
+        if (step_act_bytes(pro, m.cols, g.head_dim) > static_cast<size_t>(kStepActBytes) || !aligned(g.x) ||
+            !aligned(g.norm_w) || !aligned(g.gate_z) || !aligned(g.out) || !aligned(g.conv_w) ||
+            !aligned(g.conv_state) || (epi == kEpiConv && g.conv_k != 4) || (epi == kEpiResidual && m.rows % 4 != 0))
+            staged_ok = false;
         PhaseDesc D = {};
         D.kind = kPhaseGemv;
         D.pro = pro;
@@ -478,6 +489,7 @@ bool DeviceModel::build_phases(std::string* error) {
         g.rows_per_chunk = std::max(2, std::min(kMaxRowsPerTeam, kStepSlotBytes / m.row_stride) & ~1);
         g.stages = 0;
         g.unit = unit;
+        g.evict_first = gemv_evict_first();
         g.err = d_err_;
         D.g = g;
         return D;
@@ -596,7 +608,47 @@ bool DeviceModel::build_phases(std::string* error) {
         else n = "gemv_o_proj";
         phase_names_.push_back(n);
     }
-    phase_ns_.assign(3 * static_cast<size_t>(n_phases_), 0.0);
+    phase_ns_.assign(kStepTraceSlots * static_cast<size_t>(n_phases_), 0.0);
+    if (!staged_ok) {  // this model's shapes run on the per-op graph path instead
+        persistent_ = false;
+        return true;
+    }
+    // Tensor maps of every GEMV phase's staged vectors: [list][phase][3] in one device array.
+    {
+        const size_t per_list = static_cast<size_t>(n_phases_) * 3;
+        std::vector<uint8_t> maps(2 * per_list * kStepTmapBytes, 0);
+        cudaFree(d_tmaps_);
+        d_tmaps_ = nullptr;
+        if (cudaMalloc(&d_tmaps_, maps.size()) != cudaSuccess) {
+            *error = "tensor map allocation failed";
+            return false;
+        }
+        for (int which = 0; which < 2; ++which) {
+            std::vector<PhaseDesc>& list = which == 0 ? dec : pre;
+            for (int ph = 0; ph < n_phases_; ++ph) {
+                PhaseDesc& D = list[ph];
+                if (D.kind != kPhaseGemv) continue;
+                const GemvParams& g = D.g;
+                const float* vec[3] = {g.x, nullptr, nullptr};
+                int len[3] = {g.cols, 0, 0};
+                if (D.pro == kProRms) vec[1] = g.norm_w, len[1] = g.cols;
+                if (D.pro == kProGatedRms) vec[1] = g.gate_z, len[1] = g.cols, vec[2] = g.norm_w, len[2] = g.head_dim;
+                for (int k = 0; k < 3; ++k) {
+                    if (!vec[k]) continue;
+                    const size_t off = ((which * static_cast<size_t>(n_phases_) + ph) * 3 + k) * kStepTmapBytes;
+                    if (!encode_vector_tmap(maps.data() + off, vec[k], len[k])) {
+                        persistent_ = false;  // no tensor maps: the per-op graph path runs instead
+                        return true;
+                    }
+                    D.tmap[k] = static_cast<const uint8_t*>(d_tmaps_) + off;
+                }
+            }
+        }
+        if (cudaMemcpy(d_tmaps_, maps.data(), maps.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+            *error = "tensor map upload failed";
+            return false;
+        }
+    }
     for (int which = 0; which < 2; ++which) {
         PhaseDesc*& dst = which == 0 ? d_phases_decode_ : d_phases_prefill_;
         const std::vector<PhaseDesc>& src = which == 0 ? dec : pre;
@@ -798,6 +850,8 @@ bool DeviceModel::run_step(bool decode, std::string* error) {
         sp.phases = decode ? d_phases_decode_ : d_phases_prefill_;
         sp.nphases = n_phases_;
         sp.nslots = step_slots_;
+        sp.inflight = step_inflight_;
+        sp.l2_prefetch = step_l2_prefetch_;
         sp.grid_bar = d_grid_bar_;
         sp.err = d_err_;
         sp.prompt = d_prompt_;
@@ -808,17 +862,19 @@ bool DeviceModel::run_step(bool decode, std::string* error) {
         sp.pos = d_pos_;
         sp.next_pos = d_next_pos_;
         sp.trace = decode ? d_step_trace_ : nullptr;
+        if (sp.trace) cudaMemsetAsync(d_step_trace_, 0, kStepTraceSlots * static_cast<size_t>(n_phases_) * 8, stream_);
         const cudaError_t e = launch_decode_step(sp, meta_kind_, opts_.kv_fp16, num_sms_, stream_);
         if (e == cudaSuccess && sp.trace) {
-            std::vector<unsigned long long> t(3 * static_cast<size_t>(n_phases_));
+            std::vector<unsigned long long> t(kStepTraceSlots * static_cast<size_t>(n_phases_));
             cudaMemcpyAsync(t.data(), d_step_trace_, t.size() * 8, cudaMemcpyDeviceToHost, stream_);
             cudaStreamSynchronize(stream_);
+            constexpr int S = kStepTraceSlots;
             for (int ph = 0; ph < n_phases_; ++ph) {
-                const double start = static_cast<double>(t[3 * ph]);
-                const double prev_end = ph ? static_cast<double>(t[3 * (ph - 1) + 2]) : start;
-                phase_ns_[3 * ph] += start - prev_end;                                        // barrier latency
-                phase_ns_[3 * ph + 1] += static_cast<double>(t[3 * ph + 1]) - start;          // block 0 work
-                phase_ns_[3 * ph + 2] += static_cast<double>(t[3 * ph + 2]) - start;          // until last arrival
+                const double start = static_cast<double>(t[S * ph]);
+                const double prev_end = ph ? static_cast<double>(t[S * (ph - 1) + 2]) : start;
+                phase_ns_[S * ph] += start - prev_end;  // barrier latency
+                for (int k = 1; k < S; ++k)
+                    if (t[S * ph + k]) phase_ns_[S * ph + k] += static_cast<double>(t[S * ph + k]) - start;
             }
             ++traced_steps_;
         }
@@ -1017,21 +1073,25 @@ bool DeviceModel::logits(std::vector<float>* out, std::string* error) {
 
 std::string DeviceModel::phase_trace_summary() const {
     if (!traced_steps_) return "";
-    std::map<std::string, std::array<double, 4>> agg;
+    constexpr int S = kStepTraceSlots;
+    std::map<std::string, std::array<double, S + 1>> agg;
     for (int ph = 0; ph < n_phases_; ++ph) {
         auto& a = agg[phase_names_[ph]];
         a[0] += 1;
-        for (int k = 0; k < 3; ++k) a[k + 1] += phase_ns_[3 * ph + k] / traced_steps_;
+        for (int k = 0; k < S; ++k) a[k + 1] += phase_ns_[S * ph + k] / traced_steps_;
     }
+    // Per slot: the summed microseconds of all phases of that name, per step.
+    static const char* kSlotNames[S] = {"barrier_us",    "block0_us",     "last_arrival_us", "x_loaded_us",
+                                        "limbs_ready_us", "first_chunk_us", "loop_done_us",   "constants_staged_us"};
     std::ostringstream o;
     o << "{\"steps\":" << traced_steps_ << ",\"phases\":[";
     bool first = true;
     for (const auto& kv : agg) {
         if (!first) o << ",";
         first = false;
-        o << "{\"name\":\"" << kv.first << "\",\"count\":" << kv.second[0] << ",\"barrier_us\":"
-          << kv.second[1] / 1000.0 << ",\"block0_us\":" << kv.second[2] / 1000.0 << ",\"last_arrival_us\":"
-          << kv.second[3] / 1000.0 << "}";
+        o << "{\"name\":\"" << kv.first << "\",\"count\":" << kv.second[0];
+        for (int k = 0; k < S; ++k) o << ",\"" << kSlotNames[k] << "\":" << kv.second[k + 1] / 1000.0;
+        o << "}";
     }
     o << "]}";
     return o.str();

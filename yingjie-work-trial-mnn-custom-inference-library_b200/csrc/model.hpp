@@ -148,7 +148,10 @@ private:
     bool persistent_ = false;
     int meta_kind_ = 0;
     int step_slots_ = 0;
+    int step_inflight_ = 0;
+    int step_l2_prefetch_ = 1;
     PhaseDesc* d_phases_decode_ = nullptr;
+    void* d_tmaps_ = nullptr;  // CUtensorMap array of the phase lists
     PhaseDesc* d_phases_prefill_ = nullptr;
     int n_phases_ = 0;
     unsigned* d_grid_bar_ = nullptr;

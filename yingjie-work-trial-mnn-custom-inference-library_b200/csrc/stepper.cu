@@ -1,5 +1,7 @@
 // Persistent decode-step kernel (see stepper.cuh).
+#include <cuda.h>
 #include <cuda_fp16.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 
@@ -12,14 +14,27 @@ namespace xqb {
 namespace {
 
 // Shared-memory layout (bytes):
-//   [0, 128)     full mbarriers      [128, 256)   empty mbarriers
-//   [256, 384)   warp sums           [512, 4608)  double-buffered row sums [2][16][32]
-//   [4608, 6912) attention scratch   [6912, 8192) 3 DeltaNet scratches
-//   [8192, 8704) argmax scratch      then kStepAttnDynBytes, then the weight ring.
-constexpr int kOffFull = 0, kOffEmpty = 128, kOffWsum = 256, kOffRed = 512, kOffAttn = 4608, kOffDelta = 6912,
-              kOffArg = 8192;
+//   [0, 128)      full mbarriers       [128, 256)    empty mbarriers
+//   [256, 384)    warp sums            [384, 416)    activation / constant / 2 descriptor mbarriers
+//   [512, 4608)   double-buffered row sums [2][16][32]
+//   [4608, 6912)  attention scratch    [6912, 8192)  3 DeltaNet scratches
+//   [8192, 8704)  argmax scratch       [8704, 9728)  two phase descriptors
+//   [10240, +48K) activation area: a GEMV phase's x and its second vector (norm weights or
+//                 gate) as 128-byte rows with 128-byte swizzle, or an attention phase's q / scores
+//   [.., +4K)     epilogue inputs of this block's rows (residual, conv weights and state)
+//   then the weight ring.
+constexpr int kOffFull = 0, kOffEmpty = 128, kOffWsum = 256, kOffXBar = 384, kOffCBar = 392, kOffDBar = 400,
+              kOffRed = 512, kOffAttn = 4608, kOffDelta = 6912, kOffArg = 8192, kOffDesc = kStepHeaderBytes;
+constexpr int kDescBytes = 512;
+constexpr int kOffAct = 10240;  // 1024-byte aligned: 128-byte swizzled tensor copies land here
+constexpr int kOffEpi = kOffAct + kStepActBytes;
+constexpr int kOffRing = kOffEpi + 4 * kStepEpiFloats;
 static_assert(sizeof(AttnScratch) <= kOffDelta - kOffAttn, "attention scratch");
 static_assert(3 * sizeof(DeltaScratch) <= kOffArg - kOffDelta, "delta scratch");
+static_assert(sizeof(PhaseDesc) % 16 == 0 && sizeof(PhaseDesc) <= kDescBytes, "phase descriptor copy");
+static_assert(kStepAttnDynBytes <= kStepActBytes, "attention scratch aliases the activation area");
+static_assert(kOffRing % 128 == 0, "ring alignment");
+static_assert(kOffDesc + 2 * kDescBytes <= kOffAct && kOffAct % 1024 == 0, "activation area");
 
 struct ArgScratch {
     float v[32];
@@ -39,13 +54,25 @@ struct Ctx {
     uint8_t* base;  // dynamic shared memory
     uint64_t* full;
     uint64_t* empty;
+    uint64_t* xbar;  // activation copies of the current phase (completes once per phase)
+    uint64_t* cbar;  // constant copies of the current phase (completes once per phase)
     float* wsum;
     float* red;
+    float* act;
+    float* epi;
     uint8_t* ring;
     int nslots;
     int tid, lane, warp;
-    int gbase;  // chunks this block consumed in earlier phases
+    int gbase;   // chunks this block consumed in earlier phases
+    uint32_t parity;  // of xbar / cbar in the current phase
 };
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 __device__ __forceinline__ void block_rows(const GemvParams& p, int* r_begin, int* r_end, int* nchunks) {
     const int units = p.rows / p.unit;
@@ -54,8 +81,199 @@ __device__ __forceinline__ void block_rows(const GemvParams& p, int* r_begin, in
     *nchunks = (*r_end - *r_begin + p.rows_per_chunk - 1) / p.rows_per_chunk;
 }
 
-template <int META, int PRO, int EPI>
-__device__ __forceinline__ void gemv_phase(const GemvParams& p, Ctx& c) {
+// Rows of this block whose epilogue inputs are staged in shared memory: [r0, r1), widened to
+// multiples of 4 rows so that every copy starts and ends on a 16-byte boundary. `ok` is false
+// (inputs read from global memory instead) when they do not fit the staging area.
+struct EpiWindow {
+    int r0, r1;
+    bool ok;
+};
+__device__ __forceinline__ EpiWindow epi_window(const GemvParams& p, int epi, int r_begin, int r_end) {
+    EpiWindow w{0, 0, false};
+    if (r_begin >= r_end) return w;
+    if (epi == kEpiResidual) {
+        w.r0 = r_begin & ~3;
+        w.r1 = min(p.rows, (r_end + 3) & ~3);
+        w.ok = (p.rows & 3) == 0 && w.r1 - w.r0 <= kStepEpiFloats;
+    } else if (epi == kEpiConv && r_begin < p.conv_channels) {
+        w.r0 = r_begin & ~3;
+        w.r1 = min(p.conv_channels, (r_end + 3) & ~3);
+        w.ok = p.conv_k == 4 && (p.conv_channels & 3) == 0 && 7 * (w.r1 - w.r0) <= kStepEpiFloats;
+    }
+    return w;
+}
+
+// n fp32 values (n / 32 rows of 128 bytes) into dst by 2-D tensor copies of up to 32 rows;
+// 128-byte swizzle: the 16-byte chunk j of row r lands at chunk j ^ (r & 7).
+__device__ __forceinline__ void tma_vector(float* dst, const void* tmap, int n, uint64_t* bar) {
+    const int rows = n >> 5;
+    const int box = min(32, rows);
+    for (int r = 0; r < rows; r += box)
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+            "[%4];" ::"r"(smem_u32(dst + 32 * r)),
+            "l"(tmap), "r"(0), "r"(r), "r"(smem_u32(bar))
+            : "memory");
+}
+
+// Constant inputs of a GEMV phase (norm weights, conv weights, this block's conv state, which
+// only this block writes, in an earlier launch): issued before the grid barrier that opens the
+// phase. Always arms cbar once.
+__device__ __forceinline__ void issue_constants(const PhaseDesc& D, Ctx& c) {
+    fence_proxy_async_smem();  // the area was last read by generic loads
+    uint32_t bytes = 0;
+    const void* src[3] = {nullptr, nullptr, nullptr};
+    void* dst[3] = {nullptr, nullptr, nullptr};
+    uint32_t len[3] = {0, 0, 0};
+    int vec_n = 0, vec_map = 0;
+    float* vec_dst = nullptr;
+    if (D.kind == kPhaseGemv) {
+        const GemvParams& p = D.g;
+        if (D.pro == kProRms) {
+            vec_n = p.cols, vec_map = 1, vec_dst = c.act + p.cols;
+        } else if (D.pro == kProGatedRms) {
+            vec_n = p.head_dim, vec_map = 2, vec_dst = c.act + 2 * p.cols;
+        }
+        if (D.epi == kEpiConv) {
+            int r_begin, r_end, nchunks;
+            block_rows(p, &r_begin, &r_end, &nchunks);
+            const EpiWindow w = epi_window(p, kEpiConv, r_begin, r_end);
+            if (w.ok) {
+                const int n = w.r1 - w.r0;
+                src[1] = p.conv_w + static_cast<size_t>(w.r0) * 4, dst[1] = c.epi, len[1] = 16u * n;
+                src[2] = p.conv_state + static_cast<size_t>(w.r0) * 3, dst[2] = c.epi + 4 * n, len[2] = 12u * n;
+            }
+        }
+    }
+    for (int k = 0; k < 3; ++k) bytes += len[k];
+    mbar_expect_tx(c.cbar, bytes + 4u * vec_n);
+    if (vec_n) tma_vector(vec_dst, D.tmap[vec_map], vec_n, c.cbar);
+    for (int k = 0; k < 3; ++k)
+        if (len[k]) bulk_g2s(dst[k], src[k], len[k], c.cbar);
+}
+
+// Activation inputs of a GEMV phase (x, the gate of a gated prologue, this block's residual
+// rows): issued right after the grid barrier, whose acquire makes the other blocks' stores
+// visible; the proxy fence extends that to the bulk copies. Always arms xbar once.
+__device__ __forceinline__ void issue_activations(const PhaseDesc& D, Ctx& c) {
+    fence_proxy_async_global();
+    fence_proxy_async_smem();
+    if (D.kind != kPhaseGemv) {
+        mbar_expect_tx(c.xbar, 0);
+        return;
+    }
+    const GemvParams& p = D.g;
+    const bool gated = D.pro == kProGatedRms;
+    const void* rsrc = nullptr;
+    uint32_t rlen = 0;
+    if (D.epi == kEpiResidual) {
+        int r_begin, r_end, nchunks;
+        block_rows(p, &r_begin, &r_end, &nchunks);
+        const EpiWindow w = epi_window(p, kEpiResidual, r_begin, r_end);
+        if (w.ok) rsrc = p.out + w.r0, rlen = 4u * (w.r1 - w.r0);
+    }
+    mbar_expect_tx(c.xbar, 4u * p.cols * (gated ? 2u : 1u) + rlen);
+    tma_vector(c.act, D.tmap[0], p.cols, c.xbar);
+    if (gated) tma_vector(c.act + p.cols, D.tmap[1], p.cols, c.xbar);
+    if (rlen) bulk_g2s(c.epi, rsrc, rlen, c.xbar);
+}
+
+// One output row's epilogue with its inputs from the staging area when `w.ok`.
+template <int EPI>
+__device__ __forceinline__ void step_epilogue_row(const GemvParams& p, int r, float y, const EpiWindow& w,
+                                                  const float* epi) {
+    if constexpr (EPI == kEpiResidual) {
+        const float res = w.ok ? epi[r - w.r0] : __ldcg(p.out + r);
+        p.out[r] = res + y;  // addResidual, custom_model.cpp:294-299
+    } else if constexpr (EPI == kEpiConv) {
+        if (r < p.conv_channels && w.ok) {
+            // causal conv + SiLU + state shift, custom_model.cpp:985-1006 (conv_k = 4)
+            const int n = w.r1 - w.r0;
+            const float4 cw = *reinterpret_cast<const float4*>(epi + 4 * (r - w.r0));
+            const float* stc = epi + 4 * n + 3 * (r - w.r0);
+            const float s0 = stc[0], s1 = stc[1], s2 = stc[2];
+            float acc = 0.0f;
+            acc += s0 * cw.x;
+            acc += s1 * cw.y;
+            acc += s2 * cw.z;
+            acc += y * cw.w;
+            p.out[r] = dsilu(acc);
+            float* st = p.conv_state + static_cast<size_t>(r) * 3;
+            st[0] = s1;
+            st[1] = s2;
+            st[2] = y;
+        } else {
+            gemv_epilogue_row<EPI>(p, r, y);
+        }
+    } else {
+        gemv_epilogue_row<EPI>(p, r, y);
+    }
+}
+
+// Thread t's 32 consecutive values of a staged vector (row t of the swizzled [n/32][32] copy).
+__device__ __forceinline__ void staged_row(const float* base, int row, float (&v)[32]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 a = *reinterpret_cast<const float4*>(base + 32 * row + 4 * (i ^ (row & 7)));
+        v[4 * i] = a.x;
+        v[4 * i + 1] = a.y;
+        v[4 * i + 2] = a.z;
+        v[4 * i + 3] = a.w;
+    }
+}
+
+// gemv_load_x's arithmetic on the staged copies (same operations in the same order).
+template <int PRO>
+__device__ __forceinline__ void staged_prologue(const GemvParams& p, const float* act, int t, int lane, int warp,
+                                                int team, int wpt, int team_bar, int team_size, float* wsum,
+                                                float (&xv)[32]) {
+    staged_row(act, t, xv);
+    if constexpr (PRO == kProRms) {
+        // rmsnormReference (ref_rmsnorm.cpp:8-17): x * (1/sqrt(mean(x^2)+eps)) * w
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
+        ss = warp_sum(ss);
+        if (lane == 0) wsum[warp] = ss;
+        named_bar(team_bar, team_size);
+        float tot = 0.0f;
+        for (int w = 0; w < wpt; ++w) tot += wsum[team * wpt + w];
+        const float inv = 1.0f / sqrtf(tot / static_cast<float>(p.cols) + p.eps);
+        float g[32];
+        staged_row(act + p.cols, t, g);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) xv[i] = xv[i] * inv * g[i];
+        named_bar(team_bar, team_size);  // wsum may be reused by the next phase
+    } else if constexpr (PRO == kProGatedRms) {
+        // applyGatedHeadRms (custom_model.cpp:329-349): per head of head_dim columns,
+        // out = in * inv * w * silu(z); head_dim/32 consecutive lanes share one head.
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
+        const int tph = p.head_dim >> 5;
+        for (int o = 1; o < tph; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.head_dim) + p.eps);
+        float z[32];
+        staged_row(act + p.cols, t, z);
+        const float* wn = act + 2 * p.cols;
+        const int wr = t % tph;  // row of the staged head_dim weights
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 g = *reinterpret_cast<const float4*>(wn + 32 * wr + 4 * (i ^ (wr & 7)));
+            xv[4 * i] = xv[4 * i] * inv * g.x * dsilu(z[4 * i]);
+            xv[4 * i + 1] = xv[4 * i + 1] * inv * g.y * dsilu(z[4 * i + 1]);
+            xv[4 * i + 2] = xv[4 * i + 2] * inv * g.z * dsilu(z[4 * i + 2]);
+            xv[4 * i + 3] = xv[4 * i + 3] * inv * g.w * dsilu(z[4 * i + 3]);
+        }
+    }
+}
+
+// One GEMV phase. The prologue and epilogue kinds are runtime values (uniform branches): the
+// kernel then holds a single copy of the chunk loop, which keeps the instruction working set
+// of a step small (every phase switch would otherwise fetch a new unrolled loop).
+template <int META>
+__device__ __forceinline__ void gemv_phase(const GemvParams& p, const int pro, const int epi, Ctx& c,
+                                        unsigned long long* ts) {
     int r_begin, r_end, nchunks;
     block_rows(p, &r_begin, &r_end, &nchunks);
     const int R = p.rows_per_chunk;
@@ -64,6 +282,7 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, Ctx& c) {
     const int tid = c.tid, lane = c.lane, warp = c.warp;
     float best_v = -INFINITY;
     int best_i = (tid == 0) ? r_begin : 0x7fffffff;
+    const EpiWindow ew = epi_window(p, epi, r_begin, r_end);
     if (tid < teams * team_size) {
         const int team = tid / team_size;
         const int t = tid - team * team_size;
@@ -71,10 +290,20 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, Ctx& c) {
         const int team_bar = 2 + team;
         XLimbs L;
         {
+            mbar_wait_bounded(c.cbar, c.parity, p.err);
+            if (ts && tid == 0) ts[7] = global_ns();
+            mbar_wait_bounded(c.xbar, c.parity, p.err);
             float xv[32];
-            gemv_load_x<PRO>(p, t, lane, warp, team, wpt, team_bar, team_size, c.wsum, xv);
+            if (pro == kProRms)
+                staged_prologue<kProRms>(p, c.act, t, lane, warp, team, wpt, team_bar, team_size, c.wsum, xv);
+            else if (pro == kProGatedRms)
+                staged_prologue<kProGatedRms>(p, c.act, t, lane, warp, team, wpt, team_bar, team_size, c.wsum, xv);
+            else
+                staged_prologue<kProPlain>(p, c.act, t, lane, warp, team, wpt, team_bar, team_size, c.wsum, xv);
+            if (ts && tid == 0) ts[3] = global_ns() + (xv[0] != xv[0]);
             gemv_make_limbs<META>(xv, L);
         }
+        if (ts && tid == 0) ts[4] = global_ns();
         int it = 0;
         for (int ci = team; ci < nchunks; ci += teams, ++it) {
             const int g = c.gbase + ci;
@@ -82,6 +311,7 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, Ctx& c) {
             const int row0 = r_begin + ci * R;
             const int nr = min(R, r_end - row0);
             mbar_wait_bounded(&c.full[s], static_cast<uint32_t>((g / c.nslots) & 1), p.err);
+            if (ts && tid == 0 && it == 0) ts[5] = global_ns();
             float part[kMaxRowsPerTeam];
             gemv_chunk_partials<META, kMaxRowsPerTeam>(c.ring + static_cast<size_t>(s) * kStepSlotBytes,
                                                        p.row_stride, p.meta_offset, t, nr, L, part);
@@ -94,7 +324,7 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, Ctx& c) {
             named_bar(team_bar, team_size);
             if (t == 0) mbar_arrive(&c.empty[s]);
             const int w0 = team * wpt;
-            if constexpr (EPI == kEpiSwiglu) {
+            if (epi == kEpiSwiglu) {
                 if (t < (nr >> 1)) {
                     float gsum = 0.0f, u = 0.0f;
                     for (int w = 0; w < wpt; ++w) {
@@ -107,16 +337,21 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, Ctx& c) {
                 if (t < nr) {
                     float y = 0.0f;
                     for (int w = 0; w < wpt; ++w) y += rbuf[t * 32 + w0 + w];
-                    if constexpr (EPI == kEpiArgmax)
+                    if (epi == kEpiArgmax)
                         argmax_merge(best_v, best_i, y, row0 + t);
+                    else if (epi == kEpiResidual)
+                        step_epilogue_row<kEpiResidual>(p, row0 + t, y, ew, c.epi);
+                    else if (epi == kEpiConv)
+                        step_epilogue_row<kEpiConv>(p, row0 + t, y, ew, c.epi);
                     else
-                        gemv_epilogue_row<EPI>(p, row0 + t, y);
+                        step_epilogue_row<kEpiStore>(p, row0 + t, y, ew, c.epi);
                 }
             }
         }
     }
+    if (ts && tid == 0) ts[6] = global_ns();
     c.gbase += nchunks;
-    if constexpr (EPI == kEpiArgmax) {
+    if (epi == kEpiArgmax) {
         // Block result, then the last block merges all blocks, samples the token and loads its
         // embedding row (gemvW4A16ArgmaxNeon :309-336, loadEmbeddingRow custom_model.cpp:569-608).
         ArgScratch* a = reinterpret_cast<ArgScratch*>(c.base + kOffArg);
@@ -185,52 +420,57 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, Ctx& c) {
 }
 
 template <int META>
-__device__ __forceinline__ void gemv_dispatch(const PhaseDesc& D, Ctx& c) {
+__device__ __forceinline__ void gemv_dispatch(const PhaseDesc& D, Ctx& c, unsigned long long* ts) {
     const int pro = D.pro, epi = D.epi;
-    if (pro == kProRms && epi == kEpiConv)
-        gemv_phase<META, kProRms, kEpiConv>(D.g, c);
-    else if (pro == kProGatedRms && epi == kEpiResidual)
-        gemv_phase<META, kProGatedRms, kEpiResidual>(D.g, c);
-    else if (pro == kProRms && epi == kEpiSwiglu)
-        gemv_phase<META, kProRms, kEpiSwiglu>(D.g, c);
-    else if (pro == kProPlain && epi == kEpiResidual)
-        gemv_phase<META, kProPlain, kEpiResidual>(D.g, c);
-    else if (pro == kProRms && epi == kEpiStore)
-        gemv_phase<META, kProRms, kEpiStore>(D.g, c);
-    else if (pro == kProRms && epi == kEpiArgmax)
-        gemv_phase<META, kProRms, kEpiArgmax>(D.g, c);
+    const bool known = (pro == kProRms && (epi == kEpiConv || epi == kEpiSwiglu || epi == kEpiStore ||
+                                           epi == kEpiArgmax)) ||
+                       (pro == kProGatedRms && epi == kEpiResidual) || (pro == kProPlain && epi == kEpiResidual);
+    if (known)
+        gemv_phase<META>(D.g, pro, epi, c, ts);
     else if (c.tid == 0)
         atomicOr(D.g.err, kErrBadShape);
 }
 
 template <int META, typename KV>
 __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const StepParams P) {
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(1024) uint8_t smem[];
     Ctx c;
     c.base = smem;
     c.full = reinterpret_cast<uint64_t*>(smem + kOffFull);
     c.empty = reinterpret_cast<uint64_t*>(smem + kOffEmpty);
+    c.xbar = reinterpret_cast<uint64_t*>(smem + kOffXBar);
+    c.cbar = reinterpret_cast<uint64_t*>(smem + kOffCBar);
+    uint64_t* dbar = reinterpret_cast<uint64_t*>(smem + kOffDBar);  // [2]
     c.wsum = reinterpret_cast<float*>(smem + kOffWsum);
     c.red = reinterpret_cast<float*>(smem + kOffRed);
-    float* attn_dyn = reinterpret_cast<float*>(smem + kStepHeaderBytes);
-    c.ring = smem + kStepHeaderBytes + kStepAttnDynBytes;
+    c.act = reinterpret_cast<float*>(smem + kOffAct);
+    c.epi = reinterpret_cast<float*>(smem + kOffEpi);
+    c.ring = smem + kOffRing;
     c.nslots = P.nslots;
     c.tid = threadIdx.x;
     c.lane = c.tid & 31;
     c.warp = c.tid >> 5;
     c.gbase = 0;
+    c.parity = 0;
     if (c.tid == 0) {
         for (int s = 0; s < c.nslots; ++s) {
             mbar_init(&c.full[s], 1);
             mbar_init(&c.empty[s], 1);
         }
+        mbar_init(c.xbar, 1);
+        mbar_init(c.cbar, 1);
+        mbar_init(&dbar[0], 1);
+        mbar_init(&dbar[1], 1);
         fence_mbar_init();
+        if (smem_u32(c.act) & 1023u) atomicOr(P.err, kErrBadShape);  // swizzled copies need 1024-byte alignment
     }
     __syncthreads();
 
     if (c.warp == kStepConsumers / 32) {
         // Producer: stream this block's rows of every GEMV phase, in phase order.
         if (c.lane == 0) {
+            const int G = static_cast<int>(gridDim.x);
+            const uint64_t pol = l2_evict_first_policy();
             int g = 0;
             bool stop = false;
             for (int ph = 0; ph < P.nphases && !stop; ++ph) {
@@ -238,6 +478,19 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                 if (D.kind != kPhaseGemv) continue;
                 int r_begin, r_end, nchunks;
                 block_rows(D.g, &r_begin, &r_end, &nchunks);
+                if (P.l2_prefetch) {
+                    // Warm L2 with the phase's constant inputs well before the consumers stage them.
+                    const GemvParams& g = D.g;
+                    if (D.pro == kProRms && blockIdx.x == ph % G) prefetch_l2(g.norm_w, 4u * g.cols);
+                    if (D.pro == kProGatedRms && blockIdx.x == ph % G) prefetch_l2(g.norm_w, 4u * g.head_dim);
+                    if (D.epi == kEpiConv) {
+                        const EpiWindow w = epi_window(g, kEpiConv, r_begin, r_end);
+                        if (w.ok) {
+                            prefetch_l2(g.conv_w + static_cast<size_t>(w.r0) * 4, 16u * (w.r1 - w.r0));
+                            prefetch_l2(g.conv_state + static_cast<size_t>(w.r0) * 3, 12u * (w.r1 - w.r0));
+                        }
+                    }
+                }
                 for (int ci = 0; ci < nchunks; ++ci) {
                     const int s = g % c.nslots;
                     if (g >= c.nslots &&
@@ -245,12 +498,26 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                         stop = true;
                         break;
                     }
+                    // Keep at most `inflight` copies outstanding: more only lengthens the
+                    // memory queues that the consumers' activation loads wait in. Chunk
+                    // g - inflight is the newest copy in its slot (inflight <= nslots), so
+                    // the parity test below is unambiguous.
+                    const int old = g - P.inflight;
+                    if (old >= 0 && !mbar_wait_bounded(&c.full[old % c.nslots],
+                                                       static_cast<uint32_t>((old / c.nslots) & 1), P.err)) {
+                        stop = true;
+                        break;
+                    }
                     const int row0 = r_begin + ci * D.g.rows_per_chunk;
                     const uint32_t bytes =
                         static_cast<uint32_t>(min(D.g.rows_per_chunk, r_end - row0) * D.g.row_stride);
                     mbar_expect_tx(&c.full[s], bytes);
-                    bulk_g2s(c.ring + static_cast<size_t>(s) * kStepSlotBytes,
-                             D.g.w + static_cast<size_t>(row0) * D.g.row_stride, bytes, &c.full[s]);
+                    if (D.g.evict_first)
+                        bulk_g2s_hint(c.ring + static_cast<size_t>(s) * kStepSlotBytes,
+                                      D.g.w + static_cast<size_t>(row0) * D.g.row_stride, bytes, &c.full[s], pol);
+                    else
+                        bulk_g2s(c.ring + static_cast<size_t>(s) * kStepSlotBytes,
+                                 D.g.w + static_cast<size_t>(row0) * D.g.row_stride, bytes, &c.full[s]);
                     ++g;
                 }
             }
@@ -263,23 +530,42 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
 
     AttnScratch* ash = reinterpret_cast<AttnScratch*>(smem + kOffAttn);
     DeltaScratch* dsh = reinterpret_cast<DeltaScratch*>(smem + kOffDelta);
+    float* attn_dyn = c.act;
+    PhaseDesc* desc = reinterpret_cast<PhaseDesc*>(smem + kOffDesc);  // [2], phase ph in desc[ph & 1]
     const unsigned G = gridDim.x;
+    // Descriptor of phase ph into desc[ph & 1]; dbar[ph & 1] completes once per copy, so the
+    // copy of phase ph is its (ph >> 1)-th completion.
+    auto request_desc = [&](int ph) {
+        mbar_expect_tx(&dbar[ph & 1], static_cast<uint32_t>(sizeof(PhaseDesc)));
+        bulk_g2s(desc + (ph & 1), P.phases + ph, static_cast<uint32_t>(sizeof(PhaseDesc)), &dbar[ph & 1]);
+    };
+    auto wait_desc = [&](int ph) {
+        mbar_wait_bounded(&dbar[ph & 1], static_cast<uint32_t>((ph >> 1) & 1), P.err);
+    };
+    if (c.tid == 0) {
+        request_desc(0);
+        if (P.nphases > 1) request_desc(1);
+        wait_desc(0);
+        issue_constants(desc[0], c);
+        issue_activations(desc[0], c);  // written before this launch
+    }
     for (int ph = 0; ph < P.nphases; ++ph) {
-        const PhaseDesc& D = P.phases[ph];
-        if (ph > 0) {  // every phase consumes the previous phase's output
-            if (c.tid == 0) {
-                const unsigned target = static_cast<unsigned>(ph) * G;
-                if (ld_acquire(P.grid_bar) < target) {
-                    const uint64_t t0 = global_ns();
-                    for (uint32_t n = 1; ld_acquire(P.grid_bar) < target; ++n)
-                        if (!wait_budget_left(t0, n, P.err)) break;
-                }
+        c.parity = static_cast<uint32_t>(ph & 1);
+        if (ph > 0 && c.tid == 0) {  // every phase consumes the previous phase's output
+            const unsigned target = static_cast<unsigned>(ph) * G;
+            if (ld_acquire(P.grid_bar) < target) {
+                const uint64_t t0 = global_ns();
+                for (uint32_t n = 1; ld_acquire(P.grid_bar) < target; ++n)
+                    if (!wait_budget_left(t0, n, P.err)) break;
             }
-            named_bar(1, kStepConsumers);
+            issue_activations(desc[ph & 1], c);  // descriptor waited for at the end of phase ph - 1
         }
-        if (P.trace && blockIdx.x == 0 && c.tid == 0) P.trace[3 * ph] = global_ns();
+        named_bar(1, kStepConsumers);
+        wait_desc(ph);
+        const PhaseDesc& D = desc[ph & 1];
+        if (P.trace && blockIdx.x == 0 && c.tid == 0) P.trace[kStepTraceSlots * ph] = global_ns();
         if (D.kind == kPhaseGemv) {
-            gemv_dispatch<META>(D, c);
+            gemv_dispatch<META>(D, c, (P.trace && blockIdx.x == 0) ? P.trace + kStepTraceSlots * ph : nullptr);
         } else if (D.kind == kPhaseDelta) {
             const int nslice = D.d.dv / kDeltaCols;
             const int items = D.d.nv * nslice;
@@ -310,13 +596,29 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         }
         named_bar(1, kStepConsumers);
         if (c.tid == 0) {
-            if (P.trace && blockIdx.x == 0) P.trace[3 * ph + 1] = global_ns();
+            if (P.trace && blockIdx.x == 0) P.trace[kStepTraceSlots * ph + 1] = global_ns();
+            // Nobody reads desc[ph & 1] or the staging areas any more: stage the next phase's
+            // constants and fetch the descriptor after it, then arrive.
+            if (ph + 1 < P.nphases) {
+                wait_desc(ph + 1);
+                issue_constants(desc[(ph + 1) & 1], c);
+                if (ph + 2 < P.nphases) {
+                    fence_proxy_async_smem();
+                    request_desc(ph + 2);
+                }
+            }
             __threadfence();
             const unsigned old = atomicAdd(P.grid_bar, 1u);
-            if (P.trace && old == static_cast<unsigned>(ph + 1) * G - 1) P.trace[3 * ph + 2] = global_ns();
+            if (P.trace && old == static_cast<unsigned>(ph + 1) * G - 1) P.trace[kStepTraceSlots * ph + 2] = global_ns();
             if (ph == P.nphases - 1 && old == static_cast<unsigned>(P.nphases) * G - 1)
                 atomicExch(P.grid_bar, 0u);  // everybody has arrived; nobody waits any more
         }
+    }
+    // Copies this block issued have landed before it exits (bounded waits).
+    if (c.tid == 0 && P.nphases > 0) {
+        const int last = P.nphases - 1;
+        mbar_wait_drain(c.xbar, static_cast<uint32_t>(last & 1));
+        mbar_wait_drain(c.cbar, static_cast<uint32_t>(last & 1));
     }
 }
 
@@ -344,14 +646,14 @@ cudaError_t set_attr() {
 }  // namespace
 
 size_t step_smem_bytes(int nslots) {
-    return static_cast<size_t>(kStepHeaderBytes) + kStepAttnDynBytes + static_cast<size_t>(nslots) * kStepSlotBytes;
+    return static_cast<size_t>(kOffRing) + static_cast<size_t>(nslots) * kStepSlotBytes;
 }
 
 int step_max_slots() {
     int dev = 0, optin = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    const int avail = optin - kStepHeaderBytes - kStepAttnDynBytes - 1024;
+    const int avail = optin - kOffRing - 1024;
     return std::max(2, std::min(kStepMaxSlots, avail / kStepSlotBytes));
 }
 
@@ -361,6 +663,28 @@ cudaError_t step_init_device() {
     if ((e = set_attr<kMetaSym16, __half>()) != cudaSuccess) return e;
     if ((e = set_attr<kMetaAff32, float>()) != cudaSuccess) return e;
     return set_attr<kMetaAff32, __half>();
+}
+
+bool encode_vector_tmap(void* out, const float* ptr, int n) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            fn = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }();
+    const int rows = n / 32;
+    const int box = std::min(32, rows);
+    if (!encode || n <= 0 || n % 32 != 0 || rows % box != 0 || (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0)
+        return false;
+    const cuuint64_t dims[2] = {32, static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {128};
+    const cuuint32_t boxdim[2] = {32, static_cast<cuuint32_t>(box)};
+    const cuuint32_t estr[2] = {1, 1};
+    return encode(static_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims,
+                  strides, boxdim, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 cudaError_t launch_decode_step(const StepParams& p, int meta_kind, bool kv_fp16, int num_sms, cudaStream_t s) {

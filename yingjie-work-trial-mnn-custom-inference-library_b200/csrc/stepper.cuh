@@ -17,9 +17,13 @@ namespace xqb {
 
 enum PhaseKind : int { kPhaseGemv = 0, kPhaseDelta = 1, kPhaseAttn = 2, kPhaseEmbed = 3 };
 
-struct PhaseDesc {
+struct alignas(16) PhaseDesc {  // copied into shared memory with one bulk copy
     int kind;
     int pro, epi;
+    // kPhaseGemv: tensor maps (global memory, 128 bytes each) of x, of the second prologue
+    // vector (norm weights or gate) and of the gated norm's head_dim weights, each viewed as
+    // [n / 32][32] fp32 rows with 128-byte swizzle.
+    const void* tmap[3];
     GemvParams g;   // kPhaseGemv (rows_per_chunk and unit filled in)
     DeltaParams d;  // kPhaseDelta
     AttnParams a;   // kPhaseAttn
@@ -30,12 +34,26 @@ constexpr int kStepThreads = kStepConsumers + 32;      // + producer warp
 constexpr int kStepMaxSlots = 16;
 constexpr int kStepSlotBytes = 26112;                  // 12 rows of K=4096 or 4 rows of K=12288
 constexpr int kStepAttnDynBytes = 24 * 1024;           // q [group][hd] + scores [group][cmax]
-constexpr int kStepHeaderBytes = 8704;                 // barriers, sums, scratch (see stepper.cu)
+constexpr int kStepHeaderBytes = 8704;
+constexpr int kStepTraceSlots = 8;
+// Shared staging of a GEMV phase's inputs: x and its second vector (norm weights or gate, plus
+// the gated norm's head_dim weights) in the activation area; this block's residual rows or conv
+// weights + state in the epilogue area.
+constexpr int kStepActBytes = 48 * 1024;
+constexpr int kStepEpiFloats = 1024;
+inline size_t step_act_bytes(int pro, int cols, int head_dim) {
+    size_t b = 4u * static_cast<size_t>(cols);
+    if (pro == kProRms) b += 4u * static_cast<size_t>(cols);
+    if (pro == kProGatedRms) b += 4u * (static_cast<size_t>(cols) + static_cast<size_t>(head_dim));
+    return b;
+}                 // barriers, sums, scratch (see stepper.cu)
 
 struct StepParams {
     const PhaseDesc* phases;
     int nphases;
     int nslots;          // ring slots of kStepSlotBytes
+    int inflight;        // at most this many issued copies not yet landed (1..nslots)
+    int l2_prefetch;     // producers warm L2 with each GEMV phase's constant inputs
     unsigned* grid_bar;  // arrival counter, 0 at launch, reset to 0 by the last arrival
     unsigned* err;
     // kPhaseEmbed
@@ -46,8 +64,10 @@ struct StepParams {
     int vocab;
     int* pos;
     int* next_pos;
-    // Optional per-phase device timestamps of block 0 ([nphases][3] ns: barrier passed, work
-    // done, and — for the last block to arrive — the arrival time) when non-null.
+    // Optional per-phase device timestamps (ns), [nphases][kStepTraceSlots] when non-null:
+    // block 0 passed the barrier (0), finished its work (1), the last block arrived (2), and
+    // for GEMV phases block 0's constants staged (7), prologue done (3), activation limbs
+    // ready (4), first weight chunk landed (5), chunk loop done (6).
     unsigned long long* trace;
 };
 
@@ -58,5 +78,9 @@ size_t step_smem_bytes(int nslots);
 // Largest ring that fits next to the kernel's other shared memory on this device.
 int step_max_slots();
 cudaError_t step_init_device();
+// Tensor map (written to `out`, kStepTmapBytes) of an fp32 vector of n floats (n a multiple of
+// 32, n / 32 a multiple of min(32, n / 32)), as the step kernel stages it.
+constexpr int kStepTmapBytes = 128;
+bool encode_vector_tmap(void* out, const float* ptr, int n);
 
 }  // namespace xqb
