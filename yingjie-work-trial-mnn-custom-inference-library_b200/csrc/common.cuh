@@ -37,6 +37,10 @@ enum DeviceError : unsigned {
 // seconds instead of hanging the GPU.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 constexpr uint32_t kSpinLimit = 1u << 30;         // poll cap on top of the time limit
+#ifndef XQB_WAIT_SLEEP_NS
+#define XQB_WAIT_SLEEP_NS 0
+#endif
+constexpr uint32_t kWaitSleepHintNs = XQB_WAIT_SLEEP_NS;  // longest sleep of one mbarrier poll (0: spin)
 
 // ------------------------------------------------------------------------------------
 // PTX wrappers
@@ -100,6 +104,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// try_wait with a suspend-time hint: a waiting thread may sleep up to `hint_ns` instead of
+// spinning (it is woken when the phase completes), so waiting warps stop taking issue slots
+// from the warps that do work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -122,7 +138,8 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (kWaitSleepHintNs ? mbar_try_wait_sleep(bar, parity, kWaitSleepHintNs) : mbar_try_wait(bar, parity))
+            return true;
         if (!wait_budget_left(t0, i, err)) return false;
     }
 }

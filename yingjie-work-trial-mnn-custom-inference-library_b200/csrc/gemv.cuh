@@ -319,6 +319,8 @@ __device__ __forceinline__ void gemv_chunk_partials(const uint8_t* sb, int row_s
                                                     int nr, const XLimbs& L, float (&part)[RPT]) {
     uint4 wv[RPT];
     float sc[RPT], off[RPT];
+    // Rows jj >= nr repeat row nr - 1 (the stage may hold fewer than RPT rows); their sums only
+    // reach reduction slots of their own row index, which are never stored.
 #pragma unroll
     for (int jj = 0; jj < RPT; ++jj) {
         const uint8_t* row = sb + min(jj, nr - 1) * row_stride;
@@ -356,7 +358,7 @@ __device__ __forceinline__ void gemv_chunk_partials(const uint8_t* sb, int row_s
             val = dot * (sc[jj] * L.down) + L.nan_or_zero;
         else
             val = dot * (sc[jj] * L.down) + off[jj] * L.xsum + L.nan_or_zero;
-        part[jj] = (jj < nr) ? val : 0.0f;
+        part[jj] = val;
     }
 }
 

@@ -271,7 +271,7 @@ __device__ __forceinline__ void staged_prologue(const GemvParams& p, const float
 // One GEMV phase. The prologue and epilogue kinds are runtime values (uniform branches): the
 // kernel then holds a single copy of the chunk loop, which keeps the instruction working set
 // of a step small (every phase switch would otherwise fetch a new unrolled loop).
-template <int META>
+template <int META, int RPT>
 __device__ __forceinline__ void gemv_phase(const GemvParams& p, const int pro, const int epi, Ctx& c,
                                         unsigned long long* ts) {
     int r_begin, r_end, nchunks;
@@ -312,13 +312,13 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, const int pro, c
             const int nr = min(R, r_end - row0);
             mbar_wait_bounded(&c.full[s], static_cast<uint32_t>((g / c.nslots) & 1), p.err);
             if (ts && tid == 0 && it == 0) ts[5] = global_ns();
-            float part[kMaxRowsPerTeam];
-            gemv_chunk_partials<META, kMaxRowsPerTeam>(c.ring + static_cast<size_t>(s) * kStepSlotBytes,
-                                                       p.row_stride, p.meta_offset, t, nr, L, part);
-            const float v = reduce_rows<kMaxRowsPerTeam>(part, lane);
+            float part[RPT];
+            gemv_chunk_partials<META, RPT>(c.ring + static_cast<size_t>(s) * kStepSlotBytes, p.row_stride,
+                                           p.meta_offset, t, nr, L, part);
+            const float v = reduce_rows<RPT>(part, lane);
             float* rbuf = c.red + (it & 1) * (kMaxRowsPerChunk * 32);
-            if ((lane & (32 / kMaxRowsPerTeam - 1)) == 0) {
-                const int j = lane / (32 / kMaxRowsPerTeam);
+            if ((lane & (32 / RPT - 1)) == 0) {
+                const int j = lane / (32 / RPT);
                 if (j < nr) rbuf[j * 32 + warp] = v;
             }
             named_bar(team_bar, team_size);
@@ -425,8 +425,11 @@ __device__ __forceinline__ void gemv_dispatch(const PhaseDesc& D, Ctx& c, unsign
     const bool known = (pro == kProRms && (epi == kEpiConv || epi == kEpiSwiglu || epi == kEpiStore ||
                                            epi == kEpiArgmax)) ||
                        (pro == kProGatedRms && epi == kEpiResidual) || (pro == kProPlain && epi == kEpiResidual);
-    if (known)
-        gemv_phase<META>(D.g, pro, epi, c, ts);
+    // Chunks of 8 rows (K = 4096) or 4 rows (K = 12288): the partials loop matches the chunk.
+    if (known && D.g.rows_per_chunk == 8)
+        gemv_phase<META, 8>(D.g, pro, epi, c, ts);
+    else if (known && D.g.rows_per_chunk == 4)
+        gemv_phase<META, 4>(D.g, pro, epi, c, ts);
     else if (c.tid == 0)
         atomicOr(D.g.err, kErrBadShape);
 }
@@ -471,7 +474,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         if (c.lane == 0) {
             const int G = static_cast<int>(gridDim.x);
             const uint64_t pol = l2_evict_first_policy();
-            int g = 0;
+            int g = 0;  // chunks issued into the ring
             bool stop = false;
             for (int ph = 0; ph < P.nphases && !stop; ++ph) {
                 const PhaseDesc& D = P.phases[ph];
@@ -597,6 +600,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         named_bar(1, kStepConsumers);
         if (c.tid == 0) {
             if (P.trace && blockIdx.x == 0) P.trace[kStepTraceSlots * ph + 1] = global_ns();
+            if (P.block_done) P.block_done[static_cast<size_t>(ph) * G + blockIdx.x] = global_ns();
             // Nobody reads desc[ph & 1] or the staging areas any more: stage the next phase's
             // constants and fetch the descriptor after it, then arrive.
             if (ph + 1 < P.nphases) {
@@ -607,11 +611,18 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                     request_desc(ph + 2);
                 }
             }
-            __threadfence();
-            const unsigned old = atomicAdd(P.grid_bar, 1u);
-            if (P.trace && old == static_cast<unsigned>(ph + 1) * G - 1) P.trace[kStepTraceSlots * ph + 2] = global_ns();
-            if (ph == P.nphases - 1 && old == static_cast<unsigned>(P.nphases) * G - 1)
-                atomicExch(P.grid_bar, 0u);  // everybody has arrived; nobody waits any more
+            // Arrive. The named barrier above ordered the block's work before this thread's
+            // release; only the last phase (and a traced step) needs the counter value back.
+            if (ph == P.nphases - 1 || P.trace) {
+                unsigned old;
+                asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(P.grid_bar) : "memory");
+                if (P.trace && old == static_cast<unsigned>(ph + 1) * G - 1)
+                    P.trace[kStepTraceSlots * ph + 2] = global_ns();
+                if (ph == P.nphases - 1 && old == static_cast<unsigned>(P.nphases) * G - 1)
+                    atomicExch(P.grid_bar, 0u);  // everybody has arrived; nobody waits any more
+            } else {
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.grid_bar) : "memory");
+            }
         }
     }
     // Copies this block issued have landed before it exits (bounded waits).
