@@ -6,6 +6,8 @@ to fp16-representable values), a 512-token prefill of uniform random ids, then g
 decode steps. A "step" is one decode token. `value` is decode tok/s over the timed steps
 with everything resident in HBM (device time from CUDA events on the session stream);
 `e2e` is the same metric through xq_decode_one (host call, token copied back every step).
+`roofline` describes the dominant kernel, the persistent decode-step kernel (one launch per
+token); `gemv_kernel` the standalone W4A16 GEMV of the per-op path.
 With --gpus N (torchrun) every rank runs an independent replica session on its own GPU
 (the path does not shard for replicas); value = all ranks' tokens / max rank time.
 
@@ -107,10 +109,31 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
+def profile_figure(name, key):
+    """A per-launch figure recorded in a committed ncu summary under profiles/ (or None)."""
+    path = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(path):
+        return None
+    m = re.search(key + r":\s*([0-9.]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+def step_roofline(alg_bytes, ms_per_step, peak_gbs):
+    """The dominant kernel is the persistent decode-step kernel (one launch per token, every
+    phase of the step inside it). achieved = algorithmic bytes of one step / the mean launch
+    duration from CUDA events on the session stream over the timed region."""
+    achieved = alg_bytes / (ms_per_step * 1e-3) / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+            "frac": round(achieved / peak_gbs, 4),
+            "traffic": profile_figure("decode_step_kernel_9b.md", "traffic_bytes_per_launch"),
+            "kernel": "decode_step_kernel", "algorithmic_bytes": int(alg_bytes),
+            "launch_us": round(ms_per_step * 1000, 2)}
+
+
 def gemv_roofline(pkg, peak_gbs, iters=40):
-    """Time the dominant kernel, the fused W4A16 GEMV, at the largest per-layer shape of the
-    9B step (gate+up: 24576 x 4096) with CUDA events on the launching stream, rotating over
-    4 copies (214 MB, more than L2), and express it against the HBM roofline."""
+    """The standalone fused W4A16 GEMV kernel (the per-op path and the kernel-level C ABI) at
+    the largest per-layer shape of the 9B step (gate+up: 24576 x 4096), timed with CUDA events
+    on the launching stream, rotating over 4 copies (214 MB, more than L2)."""
     import torch
 
     rows, cols, ncopy = 24576, 4096, 4
@@ -135,16 +158,10 @@ def gemv_roofline(pkg, peak_gbs, iters=40):
     ms = e0.elapsed_time(e1) / iters
     alg = rows * cols // 2 + rows * (cols // 64) * 2 + 4 * cols + 4 * rows
     achieved = alg / (ms * 1e-3) / 1e9
-    traffic = None
-    prof = os.path.join(ROOT, "profiles", "gemv_w4a16_gate_up_9b.md")
-    if os.path.exists(prof):
-        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.]+)", open(prof).read())
-        if m:
-            traffic = float(m.group(1))
     for m in mats:
         m.close()
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
-            "frac": round(achieved / peak_gbs, 4), "traffic": traffic, "kernel": "gemv_w4a16_kernel",
+            "frac": round(achieved / peak_gbs, 4), "kernel": "gemv_w4a16_kernel",
             "shape": f"{rows}x{cols}", "algorithmic_bytes": alg, "launch_us": round(ms * 1000, 2)}
 
 
@@ -261,16 +278,24 @@ def main():
     e2e_value = world * e2e_steps / float(te.item())
 
     info = json.loads(sess.json("backend"))
+    if os.environ.get("XQ_STEP_TRACE") and rank == 0 and info.get("step_phase_trace"):
+        # per-phase device timestamps of the step kernel (slower steps: every step syncs)
+        print(json.dumps({"step_phase_trace": info["step_phase_trace"]}), file=sys.stderr, flush=True)
     kernels_per_step = int(info.get("kernels_per_decode_step", 0))
     peak, peak_kind = peaks()
-    roof = gemv_roofline(pkg, peak) if rank == 0 else None
+    gemv = gemv_roofline(pkg, peak) if rank == 0 else None
     step_bytes = info.get("weight_bytes", 0)
     if rank == 0:
+        # Algorithmic bytes of one decode step: every weight matrix once (codes + fp16 scales),
+        # the DeltaNet recurrent and conv states read and written, the KV cache read (mean
+        # context over the timed steps) and written, the embedding row.
         ctx0 = args.prompt + args.warmup
         kv_elem = 2 if args.kv_fp16 else 4
-        kv_bytes = 8 * 2 * 4 * 256 * kv_elem * (ctx0 + args.steps / 2)  # mean context over the timed steps
+        kv_bytes = 8 * 2 * 4 * 256 * kv_elem * (ctx0 + args.steps / 2 + 1)
         state_bytes = 24 * (2 * 32 * 128 * 128 * 4 + 2 * 8192 * 3 * 4)
         alg_step = step_bytes + state_bytes + kv_bytes + 4096 * 2
+        ms_step = ms_max / args.steps
+        roof = step_roofline(alg_step, ms_step, peak)
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
@@ -285,9 +310,8 @@ def main():
                        "step_execution": "persistent cooperative kernel" if info.get("persistent_step_kernel")
                        else "CUDA graph of per-op kernels with PDL"},
             "prefill_tok_s": round(prefill_tok_s, 2),
-            "step_bytes": int(alg_step),
-            "step_roofline_frac": round(alg_step / (ms_max / args.steps * 1e-3) / 1e9 / peak, 4),
-            "roofline": dict(roof, peak_kind=peak_kind) if roof else None,
+            "roofline": dict(roof, peak_kind=peak_kind),
+            "gemv_kernel": dict(gemv, peak_kind=peak_kind) if gemv else None,
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
                     "api": "xq_decode_one"},
             "gpu_launches": kernels_per_step * args.steps,
