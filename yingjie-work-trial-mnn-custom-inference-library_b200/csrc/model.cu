@@ -478,7 +478,8 @@ bool DeviceModel::build_phases(std::string* error) {
     auto gemv = [&](const DevMatrix& m, int pro, int epi, int unit, GemvParams g) {
         if (step_act_bytes(pro, m.cols, g.head_dim) > static_cast<size_t>(kStepActBytes) || !aligned(g.x) ||
             !aligned(g.norm_w) || !aligned(g.gate_z) || !aligned(g.out) || !aligned(g.conv_w) ||
-            !aligned(g.conv_state) || (epi == kEpiConv && g.conv_k != 4) || (epi == kEpiResidual && m.rows % 4 != 0))
+            !aligned(g.conv_state) || (epi == kEpiConv && g.conv_k != 4) || (epi == kEpiResidual && m.rows % 4 != 0) ||
+            (pro == kProGatedRms && (g.head_dim < 32 || m.cols / g.head_dim > 32 || 32 % (g.head_dim / 32) != 0)))
             staged_ok = false;
         PhaseDesc D = {};
         D.kind = kPhaseGemv;
@@ -885,11 +886,18 @@ bool DeviceModel::run_step(bool decode, std::string* error) {
                 std::vector<unsigned long long> bd(static_cast<size_t>(n_phases_) * G);
                 cudaMemcpy(bd.data(), d_block_done_, bd.size() * 8, cudaMemcpyDeviceToHost);
                 block_late_ns_.resize(bd.size(), 0.0);
+                barrier_ns_.resize(n_phases_, 0.0);
                 for (int ph = 0; ph < n_phases_; ++ph) {
-                    unsigned long long lo = ~0ull;
-                    for (size_t b = 0; b < G; ++b) lo = std::min(lo, bd[ph * G + b]);
+                    unsigned long long lo = ~0ull, hi = 0;
+                    for (size_t b = 0; b < G; ++b) {
+                        lo = std::min(lo, bd[ph * G + b]);
+                        hi = std::max(hi, bd[ph * G + b]);
+                    }
                     for (size_t b = 0; b < G; ++b)
                         block_late_ns_[ph * G + b] += static_cast<double>(bd[ph * G + b] - lo);
+                    // from the last block's finish to block 0 passing the next phase's barrier
+                    if (ph + 1 < n_phases_)
+                        barrier_ns_[ph] += static_cast<double>(t[S * (ph + 1)]) - static_cast<double>(hi);
                 }
             }
             ++traced_steps_;
@@ -1133,7 +1141,11 @@ std::string DeviceModel::phase_trace_summary() const {
             mean /= static_cast<double>(G) * cnt[kv.first];
             if (!f2) o << ",";
             f2 = false;
-            o << "{\"name\":\"" << kv.first << "\",\"mean_us\":" << mean / 1000.0 << ",\"latest\":[";
+            double bar = 0.0;
+            for (int ph = 0; ph < n_phases_; ++ph)
+                if (phase_names_[ph] == kv.first) bar += barrier_ns_[ph] / traced_steps_;
+            o << "{\"name\":\"" << kv.first << "\",\"mean_us\":" << mean / 1000.0
+              << ",\"last_done_to_next_start_us\":" << bar / cnt[kv.first] / 1000.0 << ",\"latest\":[";
             for (size_t k = 0; k < 6 && k < G; ++k)
                 o << (k ? "," : "") << "[" << idx[k] << "," << kv.second[idx[k]] / cnt[kv.first] / 1000.0 << "]";
             o << "]}";

@@ -154,6 +154,7 @@ private:
     void* d_tmaps_ = nullptr;  // CUtensorMap array of the phase lists
     unsigned long long* d_block_done_ = nullptr;  // XQ_STEP_TRACE >= 2: per-block phase finish times
     std::vector<double> block_late_ns_;
+    std::vector<double> barrier_ns_;
     PhaseDesc* d_phases_prefill_ = nullptr;
     int n_phases_ = 0;
     unsigned* d_grid_bar_ = nullptr;

@@ -222,6 +222,49 @@ __device__ __forceinline__ void staged_row(const float* base, int row, float (&v
     }
 }
 
+// 16-byte chunk `chunk` of row `row` of a staged [n/32][32] vector (128-byte swizzle).
+__device__ __forceinline__ float4* staged_chunk(float* base, int row, int chunk) {
+    return reinterpret_cast<float4*>(base + 32 * row + 4 * (chunk ^ (row & 7)));
+}
+
+// Gated head-RMS prologue (applyGatedHeadRms, custom_model.cpp:329-349), spread over all
+// consumers: one thread per 32-column row sums its squares and the head's lanes combine them
+// (inverse norms of the <= 32 heads in wsum), then every consumer thread normalises 16-byte
+// chunks in place, x * inv * w * silu(z) in that order. The expf work of a head lands on twelve
+// warps instead of the four that own the rows.
+__device__ __forceinline__ void gated_prologue(const GemvParams& p, Ctx& c) {
+    const int nrows = p.cols >> 5;
+    const int tph = p.head_dim >> 5;  // rows of one head: consecutive threads of one warp
+    const int tid = c.tid;
+    float ss = 0.0f;
+    if (tid < nrows) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 a = *staged_chunk(c.act, tid, i);
+            ss += a.x * a.x;
+            ss += a.y * a.y;
+            ss += a.z * a.z;
+            ss += a.w * a.w;
+        }
+    }
+    for (int o = 1; o < tph; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (tid < nrows && tid % tph == 0) c.wsum[tid / tph] = 1.0f / sqrtf(ss / static_cast<float>(p.head_dim) + p.eps);
+    named_bar(1, kStepConsumers);
+    for (int q = tid; q < nrows * 8; q += kStepConsumers) {
+        const int row = q >> 3, i = q & 7;
+        const float inv = c.wsum[row / tph];
+        float4 a = *staged_chunk(c.act, row, i);
+        const float4 z = *staged_chunk(c.act + p.cols, row, i);
+        const float4 g = *staged_chunk(c.act + 2 * p.cols, row % tph, i);
+        a.x = a.x * inv * g.x * dsilu(z.x);
+        a.y = a.y * inv * g.y * dsilu(z.y);
+        a.z = a.z * inv * g.z * dsilu(z.z);
+        a.w = a.w * inv * g.w * dsilu(z.w);
+        *staged_chunk(c.act, row, i) = a;
+    }
+    named_bar(1, kStepConsumers);  // the normalised x is visible to every team; wsum free again
+}
+
 // gemv_load_x's arithmetic on the staged copies (same operations in the same order).
 template <int PRO>
 __device__ __forceinline__ void staged_prologue(const GemvParams& p, const float* act, int t, int lane, int warp,
@@ -283,6 +326,10 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, const int pro, c
     float best_v = -INFINITY;
     int best_i = (tid == 0) ? r_begin : 0x7fffffff;
     const EpiWindow ew = epi_window(p, epi, r_begin, r_end);
+    mbar_wait_bounded(c.cbar, c.parity, p.err);
+    if (ts && tid == 0) ts[7] = global_ns();
+    mbar_wait_bounded(c.xbar, c.parity, p.err);
+    if (pro == kProGatedRms) gated_prologue(p, c);
     if (tid < teams * team_size) {
         const int team = tid / team_size;
         const int t = tid - team * team_size;
@@ -290,16 +337,11 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, const int pro, c
         const int team_bar = 2 + team;
         XLimbs L;
         {
-            mbar_wait_bounded(c.cbar, c.parity, p.err);
-            if (ts && tid == 0) ts[7] = global_ns();
-            mbar_wait_bounded(c.xbar, c.parity, p.err);
             float xv[32];
             if (pro == kProRms)
                 staged_prologue<kProRms>(p, c.act, t, lane, warp, team, wpt, team_bar, team_size, c.wsum, xv);
-            else if (pro == kProGatedRms)
-                staged_prologue<kProGatedRms>(p, c.act, t, lane, warp, team, wpt, team_bar, team_size, c.wsum, xv);
             else
-                staged_prologue<kProPlain>(p, c.act, t, lane, warp, team, wpt, team_bar, team_size, c.wsum, xv);
+                staged_row(c.act, t, xv);  // plain, or already normalised by gated_prologue
             if (ts && tid == 0) ts[3] = global_ns() + (xv[0] != xv[0]);
             gemv_make_limbs<META>(xv, L);
         }
