@@ -105,10 +105,11 @@ __device__ __forceinline__ EpiWindow epi_window(const GemvParams& p, int epi, in
 
 // n fp32 values (n / 32 rows of 128 bytes) into dst by 2-D tensor copies of up to 32 rows;
 // 128-byte swizzle: the 16-byte chunk j of row r lands at chunk j ^ (r & 7).
-__device__ __forceinline__ void tma_vector(float* dst, const void* tmap, int n, uint64_t* bar) {
+__device__ __forceinline__ void tma_vector(float* dst, const void* tmap, int n, uint64_t* bar, int lane = 0,
+                                           int lanes = 1) {
     const int rows = n >> 5;
     const int box = min(32, rows);
-    for (int r = 0; r < rows; r += box)
+    for (int r = lane * box; r < rows; r += lanes * box)
         asm volatile(
             "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
             "[%4];" ::"r"(smem_u32(dst + 32 * r)),
@@ -155,11 +156,13 @@ __device__ __forceinline__ void issue_constants(const PhaseDesc& D, Ctx& c) {
 // Activation inputs of a GEMV phase (x, the gate of a gated prologue, this block's residual
 // rows): issued right after the grid barrier, whose acquire makes the other blocks' stores
 // visible; the proxy fence extends that to the bulk copies. Always arms xbar once.
-__device__ __forceinline__ void issue_activations(const PhaseDesc& D, Ctx& c) {
+// Called by all 32 lanes of warp 0: lane 0 arms xbar with the total byte count, then the lanes
+// issue the tensor-copy boxes in parallel (a 48 KB x is 12 boxes).
+__device__ __forceinline__ void issue_activations(const PhaseDesc& D, Ctx& c, int lane) {
     fence_proxy_async_global();
     fence_proxy_async_smem();
     if (D.kind != kPhaseGemv) {
-        mbar_expect_tx(c.xbar, 0);
+        if (lane == 0) mbar_expect_tx(c.xbar, 0);
         return;
     }
     const GemvParams& p = D.g;
@@ -172,10 +175,14 @@ __device__ __forceinline__ void issue_activations(const PhaseDesc& D, Ctx& c) {
         const EpiWindow w = epi_window(p, kEpiResidual, r_begin, r_end);
         if (w.ok) rsrc = p.out + w.r0, rlen = 4u * (w.r1 - w.r0);
     }
-    mbar_expect_tx(c.xbar, 4u * p.cols * (gated ? 2u : 1u) + rlen);
-    tma_vector(c.act, D.tmap[0], p.cols, c.xbar);
-    if (gated) tma_vector(c.act + p.cols, D.tmap[1], p.cols, c.xbar);
-    if (rlen) bulk_g2s(c.epi, rsrc, rlen, c.xbar);
+    if (lane == 0) mbar_expect_tx(c.xbar, 4u * p.cols * (gated ? 2u : 1u) + rlen);
+    __syncwarp();
+    // lanes 0-15: boxes of x; lanes 16-31: boxes of the gate (n / 32 <= 512 rows: <= 16 boxes each)
+    if (lane < 16)
+        tma_vector(c.act, D.tmap[0], p.cols, c.xbar, lane, 16);
+    else if (gated)
+        tma_vector(c.act + p.cols, D.tmap[1], p.cols, c.xbar, lane - 16, 16);
+    if (rlen && lane == 31) bulk_g2s(c.epi, rsrc, rlen, c.xbar);
 }
 
 // One output row's epilogue with its inputs from the staging area when `w.ok`.
@@ -592,18 +599,25 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         if (P.nphases > 1) request_desc(1);
         wait_desc(0);
         issue_constants(desc[0], c);
-        issue_activations(desc[0], c);  // written before this launch
+    }
+    if (c.warp == 0) {
+        __syncwarp();
+        wait_desc(0);
+        issue_activations(desc[0], c, c.lane);  // written before this launch
     }
     for (int ph = 0; ph < P.nphases; ++ph) {
         c.parity = static_cast<uint32_t>(ph & 1);
-        if (ph > 0 && c.tid == 0) {  // every phase consumes the previous phase's output
-            const unsigned target = static_cast<unsigned>(ph) * G;
-            if (ld_acquire(P.grid_bar) < target) {
-                const uint64_t t0 = global_ns();
-                for (uint32_t n = 1; ld_acquire(P.grid_bar) < target; ++n)
-                    if (!wait_budget_left(t0, n, P.err)) break;
+        if (ph > 0 && c.warp == 0) {  // every phase consumes the previous phase's output
+            if (c.lane == 0) {
+                const unsigned target = static_cast<unsigned>(ph) * G;
+                if (ld_acquire(P.grid_bar) < target) {
+                    const uint64_t t0 = global_ns();
+                    for (uint32_t n = 1; ld_acquire(P.grid_bar) < target; ++n)
+                        if (!wait_budget_left(t0, n, P.err)) break;
+                }
             }
-            issue_activations(desc[ph & 1], c);  // descriptor waited for at the end of phase ph - 1
+            __syncwarp();
+            issue_activations(desc[ph & 1], c, c.lane);  // descriptor waited for at the end of phase ph - 1
         }
         named_bar(1, kStepConsumers);
         wait_desc(ph);
@@ -643,18 +657,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
         if (c.tid == 0) {
             if (P.trace && blockIdx.x == 0) P.trace[kStepTraceSlots * ph + 1] = global_ns();
             if (P.block_done) P.block_done[static_cast<size_t>(ph) * G + blockIdx.x] = global_ns();
-            // Nobody reads desc[ph & 1] or the staging areas any more: stage the next phase's
-            // constants and fetch the descriptor after it, then arrive.
-            if (ph + 1 < P.nphases) {
-                wait_desc(ph + 1);
-                issue_constants(desc[(ph + 1) & 1], c);
-                if (ph + 2 < P.nphases) {
-                    fence_proxy_async_smem();
-                    request_desc(ph + 2);
-                }
-            }
-            // Arrive. The named barrier above ordered the block's work before this thread's
-            // release; only the last phase (and a traced step) needs the counter value back.
+            // Arrive first (the named barrier above ordered the block's work before this
+            // thread's release; only the last phase, and a traced step, need the counter value
+            // back), then stage the next phase's constants and descriptor while others finish.
             if (ph == P.nphases - 1 || P.trace) {
                 unsigned old;
                 asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(P.grid_bar) : "memory");
@@ -664,6 +669,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
                     atomicExch(P.grid_bar, 0u);  // everybody has arrived; nobody waits any more
             } else {
                 asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.grid_bar) : "memory");
+            }
+            if (ph + 1 < P.nphases) {
+                wait_desc(ph + 1);
+                issue_constants(desc[(ph + 1) & 1], c);
+                if (ph + 2 < P.nphases) {
+                    fence_proxy_async_smem();
+                    request_desc(ph + 2);
+                }
             }
         }
     }
