@@ -318,6 +318,60 @@ __device__ __forceinline__ void staged_prologue(const GemvParams& p, const float
     }
 }
 
+// Partial dot products of RPT rows of a ring slot for thread t (same arithmetic as
+// gemv_chunk_partials). No row clamp: RPT rows always lie inside the slot, and the sums of rows
+// past a short last chunk are never stored.
+template <int META, int RPT>
+__device__ __forceinline__ void step_partials(const uint8_t* sb, int row_stride, int meta_offset, int t,
+                                              const XLimbs& L, float (&part)[RPT]) {
+    const uint8_t* cp = sb + 16 * t;
+    const uint8_t* mp = sb + meta_offset + (META == kMetaSym16 ? 2 : 8) * (t >> 1);
+    uint4 wv[RPT];
+    float sc[RPT], off[RPT];
+#pragma unroll
+    for (int jj = 0; jj < RPT; ++jj) {
+        wv[jj] = ld_shared_v4(cp + jj * row_stride);
+        if constexpr (META == kMetaSym16) {
+            sc[jj] = __half2float(*reinterpret_cast<const __half*>(mp + jj * row_stride));
+            off[jj] = 0.0f;
+        } else {
+            const float2 sbv = *reinterpret_cast<const float2*>(mp + jj * row_stride);
+            sc[jj] = sbv.x;
+            off[jj] = sbv.y;
+        }
+    }
+#pragma unroll
+    for (int jj = 0; jj < RPT; ++jj) {
+        const uint32_t ws[4] = {wv[jj].x, wv[jj].y, wv[jj].z, wv[jj].w};
+        int ae[3], ao[3];
+        {
+            const uint32_t lw = ws[0] & 0x0F0F0F0Fu, hw = ws[0] & 0xF0F0F0F0u;
+#pragma unroll
+            for (int l = 0; l < 3; ++l) {
+                ae[l] = dp4a_us(lw, L.le[0][l], L.acc_init[l]);
+                ao[l] = dp4a_us(hw, L.lo[0][l], 0);
+            }
+        }
+#pragma unroll
+        for (int i = 1; i < 4; ++i) {
+            const uint32_t lw = ws[i] & 0x0F0F0F0Fu, hw = ws[i] & 0xF0F0F0F0u;
+#pragma unroll
+            for (int l = 0; l < 3; ++l) {
+                ae[l] = dp4a_us(lw, L.le[i][l], ae[l]);
+                ao[l] = dp4a_us(hw, L.lo[i][l], ao[l]);
+            }
+        }
+        const float d2 = static_cast<float>(ae[2] * 16 + ao[2]);
+        const float d1 = static_cast<float>(ae[1] * 16 + ao[1]);
+        const float d0 = static_cast<float>(ae[0] * 16 + ao[0]);
+        const float dot = d2 * 65536.0f + (d1 * 256.0f + d0);
+        if constexpr (META == kMetaSym16)
+            part[jj] = dot * (sc[jj] * L.down) + L.nan_or_zero;
+        else
+            part[jj] = dot * (sc[jj] * L.down) + off[jj] * L.xsum + L.nan_or_zero;
+    }
+}
+
 // One GEMV phase. The prologue and epilogue kinds are runtime values (uniform branches): the
 // kernel then holds a single copy of the chunk loop, which keeps the instruction working set
 // of a step small (every phase switch would otherwise fetch a new unrolled loop).
@@ -354,16 +408,18 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, const int pro, c
         }
         if (ts && tid == 0) ts[4] = global_ns();
         int it = 0;
+        // ring slot and fill parity of chunk gbase + team, advanced by `teams` chunks per step
+        // (no division in the loop)
+        int s = (c.gbase + team) % c.nslots;
+        uint32_t par = static_cast<uint32_t>(((c.gbase + team) / c.nslots) & 1);
         for (int ci = team; ci < nchunks; ci += teams, ++it) {
-            const int g = c.gbase + ci;
-            const int s = g % c.nslots;
             const int row0 = r_begin + ci * R;
             const int nr = min(R, r_end - row0);
-            mbar_wait_bounded(&c.full[s], static_cast<uint32_t>((g / c.nslots) & 1), p.err);
+            mbar_wait_bounded(&c.full[s], par, p.err);
             if (ts && tid == 0 && it == 0) ts[5] = global_ns();
             float part[RPT];
-            gemv_chunk_partials<META, RPT>(c.ring + static_cast<size_t>(s) * kStepSlotBytes, p.row_stride,
-                                           p.meta_offset, t, nr, L, part);
+            step_partials<META, RPT>(c.ring + static_cast<size_t>(s) * kStepSlotBytes, p.row_stride, p.meta_offset,
+                                     t, L, part);
             const float v = reduce_rows<RPT>(part, lane);
             float* rbuf = c.red + (it & 1) * (kMaxRowsPerChunk * 32);
             if ((lane & (32 / RPT - 1)) == 0) {
@@ -372,6 +428,11 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, const int pro, c
             }
             named_bar(team_bar, team_size);
             if (t == 0) mbar_arrive(&c.empty[s]);
+            s += teams;
+            while (s >= c.nslots) {
+                s -= c.nslots;
+                par ^= 1u;
+            }
             const int w0 = team * wpt;
             if (epi == kEpiSwiglu) {
                 if (t < (nr >> 1)) {
