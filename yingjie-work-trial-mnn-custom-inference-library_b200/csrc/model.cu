@@ -376,6 +376,7 @@ bool DeviceModel::load(const std::string& dir, const Options& opts, std::string*
             if (const char* v = std::getenv("XQ_STEP_INFLIGHT")) step_inflight_ = std::atoi(v);
             step_inflight_ = std::max(1, std::min(step_inflight_, step_slots_));
             if (const char* v = std::getenv("XQ_STEP_L2_PREFETCH")) step_l2_prefetch_ = std::atoi(v) != 0;
+            if (const char* v = std::getenv("XQ_STEP_L2_AHEAD")) step_l2_ahead_ = std::max(0, std::min(64, std::atoi(v)));
             if (!build_phases(error)) return false;
             const char* tr = std::getenv("XQ_STEP_TRACE");
             if (tr && std::atoi(tr) != 0 && !dev_alloc(&d_step_trace_, kStepTraceSlots * static_cast<size_t>(n_phases_), error))
@@ -856,6 +857,7 @@ bool DeviceModel::run_step(bool decode, std::string* error) {
         sp.nslots = step_slots_;
         sp.inflight = step_inflight_;
         sp.l2_prefetch = step_l2_prefetch_;
+        sp.l2_ahead = step_l2_ahead_;
         sp.grid_bar = d_grid_bar_;
         sp.err = d_err_;
         sp.prompt = d_prompt_;
@@ -878,8 +880,13 @@ bool DeviceModel::run_step(bool decode, std::string* error) {
                 const double start = static_cast<double>(t[S * ph]);
                 const double prev_end = ph ? static_cast<double>(t[S * (ph - 1) + 2]) : start;
                 phase_ns_[S * ph] += start - prev_end;  // barrier latency
-                for (int k = 1; k < S; ++k)
-                    if (t[S * ph + k]) phase_ns_[S * ph + k] += static_cast<double>(t[S * ph + k]) - start;
+                for (int k = 1; k < S; ++k) {
+                    if (!t[S * ph + k]) continue;
+                    if (k >= 8)
+                        phase_ns_[S * ph + k] += static_cast<double>(t[S * ph + k]);  // durations
+                    else
+                        phase_ns_[S * ph + k] += static_cast<double>(t[S * ph + k]) - start;
+                }
             }
             if (sp.block_done) {
                 const size_t G = static_cast<size_t>(num_sms_);
@@ -1106,7 +1113,8 @@ std::string DeviceModel::phase_trace_summary() const {
     }
     // Per slot: the summed microseconds of all phases of that name, per step.
     static const char* kSlotNames[S] = {"barrier_us",    "block0_us",     "last_arrival_us", "x_loaded_us",
-                                        "limbs_ready_us", "first_chunk_us", "loop_done_us",   "constants_staged_us"};
+                                        "limbs_ready_us", "first_chunk_us", "loop_done_us",   "constants_staged_us",
+                                        "chunk_wait_us", "producer_slot_wait_us"};
     std::ostringstream o;
     o << "{\"steps\":" << traced_steps_ << ",\"phases\":[";
     bool first = true;

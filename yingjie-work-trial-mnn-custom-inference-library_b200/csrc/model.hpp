@@ -150,6 +150,7 @@ private:
     int step_slots_ = 0;
     int step_inflight_ = 0;
     int step_l2_prefetch_ = 1;
+    int step_l2_ahead_ = 0;  // chunks (XQ_STEP_L2_AHEAD); prefetching into L2 measured slower
     PhaseDesc* d_phases_decode_ = nullptr;
     void* d_tmaps_ = nullptr;  // CUtensorMap array of the phase lists
     unsigned long long* d_block_done_ = nullptr;  // XQ_STEP_TRACE >= 2: per-block phase finish times

@@ -35,7 +35,7 @@ constexpr int kStepMaxSlots = 16;
 constexpr int kStepSlotBytes = 26112;                  // 12 rows of K=4096 or 4 rows of K=12288
 constexpr int kStepAttnDynBytes = 24 * 1024;           // q [group][hd] + scores [group][cmax]
 constexpr int kStepHeaderBytes = 8704;
-constexpr int kStepTraceSlots = 8;
+constexpr int kStepTraceSlots = 10;
 // Shared staging of a GEMV phase's inputs: x and its second vector (norm weights or gate, plus
 // the gated norm's head_dim weights) in the activation area; this block's residual rows or conv
 // weights + state in the epilogue area.
@@ -54,6 +54,7 @@ struct StepParams {
     int nslots;          // ring slots of kStepSlotBytes
     int inflight;        // at most this many issued copies not yet landed (1..nslots)
     int l2_prefetch;     // producers warm L2 with each GEMV phase's constant inputs
+    int l2_ahead;        // weight chunks prefetched into L2 ahead of the ring, within a phase
     unsigned* grid_bar;  // arrival counter, 0 at launch, reset to 0 by the last arrival
     unsigned* err;
     // kPhaseEmbed
@@ -67,7 +68,9 @@ struct StepParams {
     // Optional per-phase device timestamps (ns), [nphases][kStepTraceSlots] when non-null:
     // block 0 passed the barrier (0), finished its work (1), the last block arrived (2), and
     // for GEMV phases block 0's constants staged (7), prologue done (3), activation limbs
-    // ready (4), first weight chunk landed (5), chunk loop done (6).
+    // ready (4), first weight chunk landed (5), chunk loop done (6); and two durations (ns):
+    // thread 0's time waiting for weight chunks to land (8), the producer's time waiting for
+    // free ring slots while issuing this phase's chunks (9).
     unsigned long long* trace;
     // Optional [nphases][gridDim.x] time (ns) at which each block finished its part of a phase.
     unsigned long long* block_done;
