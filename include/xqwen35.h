@@ -122,6 +122,23 @@ XQ_API xq_status xq_create_cuda(const char* model_dir,
  * Session metrics advance as for n xq_decode_one calls. */
 XQ_API xq_status xq_cuda_decode_timed(xq_session* session, size_t n, int32_t* tokens, double* device_ms);
 
+/* ---- Session snapshot / restore (no reference counterpart; the reference only has
+ * xq_reset, session.cpp:505-525) ---------------------------------------------------
+ * A snapshot holds everything a later decode step reads: the position, the hidden state the
+ * next step samples from, every DeltaNet layer's conv and recurrent state and every attention
+ * layer's KV cache up to the position, in a self-describing host buffer (header + raw state).
+ * Use it to cache a prompt prefix: prefill once, save, then restore it into this or another
+ * session of the same model (same shapes and KV precision) and decode from there.
+ *   xq_snapshot_size:    bytes a snapshot of the current state needs.
+ *   xq_snapshot_save:    write it; XQ_ERR_BUFFER_TOO_SMALL (with *written = bytes needed)
+ *                        if capacity is short; XQ_ERR_NOT_READY before a prefill.
+ *   xq_snapshot_restore: replace the session's state; XQ_ERR_INVALID_ARGUMENT if the buffer
+ *                        is not a snapshot of a model of this shape / KV type. Afterwards the
+ *                        session decodes exactly as it would have after the saved state. */
+XQ_API xq_status xq_snapshot_size(xq_session* session, size_t* bytes);
+XQ_API xq_status xq_snapshot_save(xq_session* session, void* buffer, size_t capacity, size_t* written);
+XQ_API xq_status xq_snapshot_restore(xq_session* session, const void* buffer, size_t size);
+
 #ifdef __cplusplus
 }
 #endif

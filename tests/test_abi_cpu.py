@@ -47,6 +47,10 @@ def test_null_arguments_follow_reference_status_codes():
     assert L.xq_get_last_metrics(None, None) == PKG.XQ_ERR_INVALID_ARGUMENT
     n = C.c_size_t()
     assert L.xq_get_hidden_state(None, None, 0, C.byref(n)) == PKG.XQ_ERR_INVALID_ARGUMENT
+    # snapshot entry points (no reference counterpart) follow the same conventions
+    assert L.xq_snapshot_size(None, C.byref(n)) == PKG.XQ_ERR_INVALID_ARGUMENT
+    assert L.xq_snapshot_save(None, None, 0, C.byref(n)) == PKG.XQ_ERR_INVALID_ARGUMENT
+    assert L.xq_snapshot_restore(None, None, 0) == PKG.XQ_ERR_INVALID_ARGUMENT
     L.xq_destroy(None)
 
 

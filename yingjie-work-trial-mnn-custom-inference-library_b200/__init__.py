@@ -30,6 +30,7 @@ ABI_SYMBOLS = [
     "xq_create", "xq_destroy", "xq_prefill", "xq_decode_one", "xq_generate", "xq_reset",
     "xq_get_last_metrics", "xq_get_backend_info", "xq_get_kernel_trace_json", "xq_get_debug_json",
     "xq_get_hidden_state", "xq_run_vulkan_w4a16_selftest", "xq_create_cuda", "xq_cuda_decode_timed",
+    "xq_snapshot_size", "xq_snapshot_save", "xq_snapshot_restore",
 ]
 KERNEL_SYMBOLS = [
     "xqk_last_error", "xqk_matrix_create", "xqk_matrix_destroy", "xqk_matrix_info", "xqk_gemv_w4a16",
@@ -91,6 +92,9 @@ def lib():
     L.xq_get_hidden_state.argtypes = [P, C.POINTER(C.c_float), C.c_size_t, C.POINTER(C.c_size_t)]
     L.xq_run_vulkan_w4a16_selftest.argtypes = [C.c_char_p, C.c_size_t]
     L.xq_cuda_decode_timed.argtypes = [P, C.c_size_t, C.POINTER(C.c_int32), C.POINTER(C.c_double)]
+    L.xq_snapshot_size.argtypes = [P, C.POINTER(C.c_size_t)]
+    L.xq_snapshot_save.argtypes = [P, P, C.c_size_t, C.POINTER(C.c_size_t)]
+    L.xq_snapshot_restore.argtypes = [P, P, C.c_size_t]
     L.xqk_last_error.restype = C.c_char_p
     L.xqk_matrix_create.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(P)]
     L.xqk_matrix_destroy.argtypes = [P]
@@ -228,6 +232,24 @@ class Session:
         if st != XQ_OK:
             raise RuntimeError(f"xq_cuda_decode_timed failed: {st}")
         return ms.value, (toks[:n] if want_tokens else None)
+
+    def snapshot(self) -> bytes:
+        """The session's decode state (xq_snapshot_save) as bytes."""
+        n = C.c_size_t()
+        st = self.L.xq_snapshot_size(self.h, C.byref(n))
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_snapshot_size failed: {st}")
+        buf = C.create_string_buffer(n.value)
+        w = C.c_size_t()
+        st = self.L.xq_snapshot_save(self.h, buf, n.value, C.byref(w))
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_snapshot_save failed: {st}")
+        return buf.raw[: w.value]
+
+    def restore(self, snap: bytes) -> int:
+        """Replace the session's state with a snapshot (xq_snapshot_restore); returns the status."""
+        buf = C.create_string_buffer(snap, len(snap))
+        return self.L.xq_snapshot_restore(self.h, buf, len(snap))
 
     def metrics(self) -> XqMetrics:
         m = self._m()

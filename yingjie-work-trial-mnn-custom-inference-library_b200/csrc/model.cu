@@ -1102,6 +1102,133 @@ bool DeviceModel::logits(std::vector<float>* out, std::string* error) {
     return true;
 }
 
+namespace {
+struct SnapshotHeader {
+    char magic[8];  // "XQSNAP1\0"
+    uint32_t version, kv_elem;
+    int32_t position, pos, next_pos, reserved0;
+    uint32_t layers, hidden, conv_dim, conv_k, lv_heads, lk_hd, lv_hd, kv_heads, head_dim, full_layers;
+    uint64_t bytes;
+};
+constexpr char kSnapMagic[8] = {'X', 'Q', 'S', 'N', 'A', 'P', '1', '\0'};
+}  // namespace
+
+size_t DeviceModel::snapshot_bytes() const {
+    const size_t conv = static_cast<size_t>(d_.conv_dim) * std::max(0, d_.conv_k - 1);
+    const size_t rec = static_cast<size_t>(d_.lv_heads) * d_.lk_hd * d_.lv_hd;
+    const size_t kv = static_cast<size_t>(position_) * d_.kv_heads * d_.head_dim * (opts_.kv_fp16 ? 2 : 4);
+    size_t b = sizeof(SnapshotHeader) + sizeof(float) * static_cast<size_t>(d_.hidden);
+    for (const DevLayer& L : layers_) b += L.full ? 2 * kv : sizeof(float) * (conv + rec);
+    return b;
+}
+
+bool DeviceModel::save_snapshot(void* buf, size_t cap, size_t* written, std::string* error) {
+    const size_t need = snapshot_bytes();
+    if (written) *written = need;
+    if (!buf || cap < need) {
+        *error = "snapshot buffer too small";
+        return false;
+    }
+    SnapshotHeader h = {};
+    std::memcpy(h.magic, kSnapMagic, 8);
+    h.version = 1;
+    h.kv_elem = opts_.kv_fp16 ? 2 : 4;
+    h.position = position_;
+    h.layers = static_cast<uint32_t>(layers_.size());
+    h.hidden = d_.hidden, h.conv_dim = d_.conv_dim, h.conv_k = d_.conv_k, h.lv_heads = d_.lv_heads;
+    h.lk_hd = d_.lk_hd, h.lv_hd = d_.lv_hd, h.kv_heads = d_.kv_heads, h.head_dim = d_.head_dim;
+    for (const DevLayer& L : layers_) h.full_layers += L.full ? 1 : 0;
+    h.bytes = need;
+    uint8_t* p = static_cast<uint8_t*>(buf) + sizeof h;
+    auto get = [&](const void* src, size_t bytes) {
+        const cudaError_t e = cudaMemcpyAsync(p, src, bytes, cudaMemcpyDeviceToHost, stream_);
+        p += bytes;
+        return e == cudaSuccess;
+    };
+    int32_t dev_pos[2] = {0, 0};  // device positions, written to the header once they arrive
+    bool ok = cudaMemcpyAsync(dev_pos, d_pos_, 4, cudaMemcpyDeviceToHost, stream_) == cudaSuccess &&
+              cudaMemcpyAsync(dev_pos + 1, d_next_pos_, 4, cudaMemcpyDeviceToHost, stream_) == cudaSuccess;
+    ok = ok && get(d_hidden_, sizeof(float) * d_.hidden);
+    const size_t conv = static_cast<size_t>(d_.conv_dim) * std::max(0, d_.conv_k - 1);
+    const size_t rec = static_cast<size_t>(d_.lv_heads) * d_.lk_hd * d_.lv_hd;
+    const size_t kv = static_cast<size_t>(position_) * d_.kv_heads * d_.head_dim * h.kv_elem;
+    for (const DevLayer& L : layers_) {
+        if (L.full)
+            ok = ok && get(L.k_cache, kv) && get(L.v_cache, kv);
+        else
+            ok = ok && get(L.conv_state, sizeof(float) * conv) && get(L.rec_state, sizeof(float) * rec);
+    }
+    ok = ok && cudaStreamSynchronize(stream_) == cudaSuccess;
+    if (!ok) {
+        *error = std::string("snapshot copy failed: ") + cudaGetErrorString(cudaGetLastError());
+        return false;
+    }
+    h.pos = dev_pos[0];
+    h.next_pos = dev_pos[1];
+    std::memcpy(buf, &h, sizeof h);
+    return true;
+}
+
+bool DeviceModel::restore_snapshot(const void* buf, size_t size, std::string* error, bool* invalid) {
+    *invalid = true;
+    SnapshotHeader h;
+    if (!buf || size < sizeof h) {
+        *error = "snapshot too small";
+        return false;
+    }
+    std::memcpy(&h, buf, sizeof h);
+    uint32_t full = 0;
+    for (const DevLayer& L : layers_) full += L.full ? 1 : 0;
+    if (std::memcmp(h.magic, kSnapMagic, 8) != 0 || h.version != 1) {
+        *error = "not a snapshot of this library";
+        return false;
+    }
+    if (h.kv_elem != (opts_.kv_fp16 ? 2u : 4u) || h.layers != layers_.size() || h.full_layers != full ||
+        h.hidden != static_cast<uint32_t>(d_.hidden) || h.conv_dim != static_cast<uint32_t>(d_.conv_dim) ||
+        h.conv_k != static_cast<uint32_t>(d_.conv_k) || h.lv_heads != static_cast<uint32_t>(d_.lv_heads) ||
+        h.lk_hd != static_cast<uint32_t>(d_.lk_hd) || h.lv_hd != static_cast<uint32_t>(d_.lv_hd) ||
+        h.kv_heads != static_cast<uint32_t>(d_.kv_heads) || h.head_dim != static_cast<uint32_t>(d_.head_dim) ||
+        h.position < 0 || h.next_pos != h.position) {
+        *error = "snapshot does not match this model (shape, KV type or positions)";
+        return false;
+    }
+    const size_t conv = static_cast<size_t>(d_.conv_dim) * std::max(0, d_.conv_k - 1);
+    const size_t rec = static_cast<size_t>(d_.lv_heads) * d_.lk_hd * d_.lv_hd;
+    const size_t kv = static_cast<size_t>(h.position) * d_.kv_heads * d_.head_dim * h.kv_elem;
+    const size_t need = sizeof h + sizeof(float) * static_cast<size_t>(d_.hidden) +
+                        static_cast<size_t>(full) * 2 * kv + (layers_.size() - full) * sizeof(float) * (conv + rec);
+    if (size < need || h.bytes != need) {
+        *error = "snapshot size does not match its header";
+        return false;
+    }
+    *invalid = false;
+    if (!ensure_capacity(std::max(1, h.position), error)) return false;
+    const uint8_t* p = static_cast<const uint8_t*>(buf) + sizeof h;
+    auto put = [&](void* dst, size_t bytes) {
+        const cudaError_t e = cudaMemcpyAsync(dst, p, bytes, cudaMemcpyHostToDevice, stream_);
+        p += bytes;
+        return e == cudaSuccess;
+    };
+    bool ok = cudaMemcpyAsync(d_pos_, &h.pos, 4, cudaMemcpyHostToDevice, stream_) == cudaSuccess &&
+              cudaMemcpyAsync(d_next_pos_, &h.next_pos, 4, cudaMemcpyHostToDevice, stream_) == cudaSuccess;
+    ok = ok && put(d_hidden_, sizeof(float) * d_.hidden);
+    for (DevLayer& L : layers_) {
+        if (L.full)
+            ok = ok && put(L.k_cache, kv) && put(L.v_cache, kv);
+        else
+            ok = ok && put(L.conv_state, sizeof(float) * conv) && put(L.rec_state, sizeof(float) * rec);
+    }
+    ok = ok && cudaMemsetAsync(d_ring_ctr_, 0, sizeof(int), stream_) == cudaSuccess;
+    ok = ok && cudaStreamSynchronize(stream_) == cudaSuccess;
+    if (!ok) {
+        *error = std::string("snapshot restore failed: ") + cudaGetErrorString(cudaGetLastError());
+        return false;
+    }
+    position_ = h.position;
+    ring_count_ = 0;
+    return true;
+}
+
 std::string DeviceModel::phase_trace_summary() const {
     if (!traced_steps_) return "";
     constexpr int S = kStepTraceSlots;

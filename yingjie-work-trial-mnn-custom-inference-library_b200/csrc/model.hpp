@@ -76,6 +76,13 @@ public:
     bool hidden(std::vector<float>* out, std::string* error);
     // Full lm_head logits of the current (normed) hidden state, for debug JSON.
     bool logits(std::vector<float>* out, std::string* error);
+    // Decode-state snapshot (no reference counterpart): positions, the hidden state the next
+    // step samples from, DeltaNet conv + recurrent states, and the KV cache up to the position,
+    // in a self-describing host buffer. Restoring needs a model of the same shape and KV type.
+    size_t snapshot_bytes() const;
+    bool save_snapshot(void* buf, size_t cap, size_t* written, std::string* error);
+    // *invalid is set when the buffer is not a snapshot of a model of this shape / KV type.
+    bool restore_snapshot(const void* buf, size_t size, std::string* error, bool* invalid);
     // Device error word set by bounded waits; 0 when clean.
     unsigned device_errors();
 
