@@ -77,6 +77,8 @@ def test_status_codes_and_trace(small_pkg):
                "sampling_greedy_custom"]:  # the rows test_runtime.cpp:175-202 requires
         assert n_ in names
     assert "fallback_" not in trace
+    m2 = s.metrics()
+    assert m2.rss_kb > 0 and m2.pss_kb > 0  # host resident set; device memory of the session
     info = s.json("backend")
     assert "full_custom_decode=true" in info and "fallback_ops=none" in info
     dbg = json.loads(s.json("debug"))
@@ -84,6 +86,28 @@ def test_status_codes_and_trace(small_pkg):
     assert s.reset() == 0
     assert L.xq_decode_one(s.h, C.byref(t), C.byref(m)) == PKG.XQ_ERR_NOT_READY
     s.close()
+
+
+def test_step_phase_trace_rows(small_pkg, monkeypatch):
+    """With XQ_STEP_TRACE=1 the kernel trace carries one row per step-kernel phase kind with its
+    device time, under names the reference's op_family rules classify."""
+    monkeypatch.setenv("XQ_STEP_TRACE", "1")
+    s = PKG.Session(small_pkg, device=0)
+    try:
+        if not json.loads(s.json("backend")).get("persistent_step_kernel"):
+            pytest.skip("model not served by the step kernel")
+        s.prefill(np.arange(9, dtype=np.int32))
+        for _ in range(3):
+            s.decode_one()
+        rows = {r["name"]: r for r in json.loads(s.json("trace"))["rows"]}
+        r = rows["linear_gate_proj_up_proj_swiglu_step_phase"]
+        assert r["backend"] == "cuda_persistent_kernel" and r["op_family"] == "gate_proj"
+        assert r["calls"] > 0 and r["total_ms"] > 0
+        assert rows["lm_head_argmax_step_phase"]["op_family"] == "lm_head"
+        assert rows["linear_attention_state_step_phase"]["op_family"] == "linear_attention_state"
+        assert rows["decode_step_custom"]["backend"] == "cuda_persistent_kernel"
+    finally:
+        s.close()
 
 
 def test_fp16_kv_cache_tolerance(small_pkg):

@@ -1229,6 +1229,20 @@ bool DeviceModel::restore_snapshot(const void* buf, size_t size, std::string* er
     return true;
 }
 
+std::vector<DeviceModel::PhaseTime> DeviceModel::phase_times() const {
+    std::vector<PhaseTime> out;
+    if (!traced_steps_) return out;
+    constexpr int S = kStepTraceSlots;
+    std::map<std::string, std::pair<int, double>> agg;
+    for (int ph = 0; ph < n_phases_; ++ph) {
+        auto& a = agg[phase_names_[ph]];
+        a.first += 1;
+        a.second += (phase_ns_[S * ph] + phase_ns_[S * ph + 2]) / traced_steps_ / 1000.0;  // barrier + phase
+    }
+    for (const auto& kv : agg) out.push_back({kv.first, kv.second.first, traced_steps_, kv.second.second});
+    return out;
+}
+
 std::string DeviceModel::phase_trace_summary() const {
     if (!traced_steps_) return "";
     constexpr int S = kStepTraceSlots;

@@ -174,6 +174,15 @@ private:
 public:
     // Per-phase device time summary of the persistent kernel (empty unless tracing).
     std::string phase_trace_summary() const;
+    // Per phase name: (phases per step, traced steps, summed device us per step from the phase
+    // start to its last block's arrival); empty unless XQ_STEP_TRACE recorded steps.
+    struct PhaseTime {
+        std::string name;
+        int per_step;
+        int steps;
+        double us_per_step;
+    };
+    std::vector<PhaseTime> phase_times() const;
 
 private:
 };

@@ -5,6 +5,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <fstream>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -403,7 +404,28 @@ public:
 
     xq_status trace_json(char* buf, size_t cap) const {
         if (!buf || cap == 0) return XQ_ERR_INVALID_ARGUMENT;
-        return copy_json(trace_.json(), buf, cap);
+        if (!model_ || !model_->persistent() || model_->phase_times().empty()) return copy_json(trace_.json(), buf, cap);
+        // With the step-kernel phase trace on (XQ_STEP_TRACE), add one row per phase kind with
+        // its measured device time, named so the reference's op_family rules classify it.
+        Trace t = trace_;
+        static const std::map<std::string, std::string> rows = {
+            {"lm_head_argmax", "lm_head_argmax_step_phase"},
+            {"gemv_in_proj_conv", "linear_attn_in_proj_conv_step_phase"},
+            {"delta", "linear_attention_state_step_phase"},
+            {"gemv_out_proj", "linear_attn_out_proj_gated_rms_step_phase"},
+            {"gemv_qkv", "linear_q_proj_k_v_step_phase"},
+            {"attention", "attention_decode_step_phase"},
+            {"gemv_o_proj", "linear_o_proj_step_phase"},
+            {"gemv_gate_up", "linear_gate_proj_up_proj_swiglu_step_phase"},
+            {"gemv_down", "linear_down_proj_step_phase"},
+            {"embed", "embedding_load_step_phase"}};
+        for (const auto& pt : model_->phase_times()) {
+            const auto it = rows.find(pt.name);
+            const std::string name = it != rows.end() ? it->second : pt.name + "_step_phase";
+            t.add(name, static_cast<uint64_t>(pt.per_step) * pt.steps, pt.us_per_step * pt.steps / 1000.0,
+                  "cuda_persistent_kernel");
+        }
+        return copy_json(t.json(), buf, cap);
     }
 
     // debugJson (custom_model.cpp:1382-1436): hidden statistics + top-10 lm_head logits.
@@ -469,7 +491,17 @@ private:
         return XQ_OK;
     }
     void set_error(const std::string& m) { copy_string(metrics_.error, sizeof metrics_.error, m); }
+    // The reference declares rss_kb / pss_kb and leaves them 0; here rss_kb is the host
+    // process's resident set (VmRSS) and pss_kb the device memory this session holds.
+    void update_memory() {
+        std::ifstream f("/proc/self/status");
+        std::string line;
+        while (std::getline(f, line))
+            if (line.rfind("VmRSS:", 0) == 0) metrics_.rss_kb = std::strtoull(line.c_str() + 6, nullptr, 10);
+        if (model_) metrics_.pss_kb = model_->device_bytes() / 1024;
+    }
     void update_rates() {  // session.cpp:595-602
+        update_memory();
         metrics_.prefill_tokens_per_second =
             metrics_.prefill_ms > 0.0 ? static_cast<double>(metrics_.prompt_tokens) * 1000.0 / metrics_.prefill_ms : 0.0;
         metrics_.decode_tokens_per_second =
@@ -491,7 +523,7 @@ private:
     }
     void trace_step_ops(uint64_t steps, bool decode) {
         if (!model_) return;
-        const std::string b = cuda_.use_graphs ? "cuda_graph" : "cuda";
+        const std::string b = step_backend();
         int full = 0, lin = 0;
         for (const DevLayer& L : model_->layers()) (L.full ? full : lin) += 1;
         if (decode) {
@@ -528,12 +560,16 @@ private:
         }
         trace_.add("rmsnorm_final", steps, 0.0, b);
     }
+    std::string step_backend() const {
+        if (model_ && model_->persistent()) return "cuda_persistent_kernel";
+        return cuda_.use_graphs ? "cuda_graph" : "cuda";
+    }
     void trace_prefill(uint64_t n, double ms) {
-        trace_.add("prefill_token_custom", n, ms, cuda_.use_graphs ? "cuda_graph" : "cuda");
+        trace_.add("prefill_token_custom", n, ms, step_backend());
         trace_step_ops(n, false);
     }
     void trace_decode(uint64_t n, double ms) {
-        trace_.add("decode_step_custom", n, ms, cuda_.use_graphs ? "cuda_graph" : "cuda");
+        trace_.add("decode_step_custom", n, ms, step_backend());
         trace_step_ops(n, true);
     }
 
