@@ -135,6 +135,16 @@ XQ_API xq_status xq_cuda_decode_timed(xq_session* session, size_t n, int32_t* to
  *   xq_snapshot_restore: replace the session's state; XQ_ERR_INVALID_ARGUMENT if the buffer
  *                        is not a snapshot of a model of this shape / KV type. Afterwards the
  *                        session decodes exactly as it would have after the saved state. */
+/* ---- Packed B200 weight layout (no reference counterpart; an addition next to the
+ * reference's packer, customlib/packer/pack_qwen35_xq4_numpy.py:191-268) ------------------
+ * Write every fused weight matrix of the package in model_dir in the kernels' row layout to
+ * model_dir/b200/<name>.b200 and model_dir/b200/layout.json. Runs on the host only (no GPU).
+ * xq_create then reads those files instead of re-tiling the xq4 files (their shapes are still
+ * checked against the manifest); deleting b200/layout.json returns to the xq4 path.
+ * XQ_ERR_INVALID_ARGUMENT for a null dir, XQ_ERR_MODEL (message in error_out) for package
+ * problems. */
+XQ_API xq_status xq_pack_b200_layout(const char* model_dir, char* error_out, size_t error_capacity);
+
 XQ_API xq_status xq_snapshot_size(xq_session* session, size_t* bytes);
 XQ_API xq_status xq_snapshot_save(xq_session* session, void* buffer, size_t capacity, size_t* written);
 XQ_API xq_status xq_snapshot_restore(xq_session* session, const void* buffer, size_t size);

@@ -30,7 +30,7 @@ ABI_SYMBOLS = [
     "xq_create", "xq_destroy", "xq_prefill", "xq_decode_one", "xq_generate", "xq_reset",
     "xq_get_last_metrics", "xq_get_backend_info", "xq_get_kernel_trace_json", "xq_get_debug_json",
     "xq_get_hidden_state", "xq_run_vulkan_w4a16_selftest", "xq_create_cuda", "xq_cuda_decode_timed",
-    "xq_snapshot_size", "xq_snapshot_save", "xq_snapshot_restore",
+    "xq_snapshot_size", "xq_snapshot_save", "xq_snapshot_restore", "xq_pack_b200_layout",
 ]
 KERNEL_SYMBOLS = [
     "xqk_last_error", "xqk_matrix_create", "xqk_matrix_destroy", "xqk_matrix_info", "xqk_gemv_w4a16",
@@ -93,6 +93,7 @@ def lib():
     L.xq_run_vulkan_w4a16_selftest.argtypes = [C.c_char_p, C.c_size_t]
     L.xq_cuda_decode_timed.argtypes = [P, C.c_size_t, C.POINTER(C.c_int32), C.POINTER(C.c_double)]
     L.xq_snapshot_size.argtypes = [P, C.POINTER(C.c_size_t)]
+    L.xq_pack_b200_layout.argtypes = [C.c_char_p, C.c_char_p, C.c_size_t]
     L.xq_snapshot_save.argtypes = [P, P, C.c_size_t, C.POINTER(C.c_size_t)]
     L.xq_snapshot_restore.argtypes = [P, P, C.c_size_t]
     L.xqk_last_error.restype = C.c_char_p
@@ -120,6 +121,14 @@ def last_error() -> str:
 def check(rc: int, what: str) -> None:
     if rc != 0:
         raise RuntimeError(f"{what} failed ({rc}): {last_error()}")
+
+
+def pack_b200(model_dir: str) -> None:
+    """Write the package's weights in the kernels' row layout (xq_pack_b200_layout; host only)."""
+    err = C.create_string_buffer(1024)
+    st = lib().xq_pack_b200_layout(model_dir.encode(), err, len(err))
+    if st != XQ_OK:
+        raise RuntimeError(f"xq_pack_b200_layout failed: {st} {err.value.decode()}")
 
 
 class Matrix:

@@ -138,7 +138,36 @@ bool upload_matrix(const std::vector<const HostMatrix*>& parts, bool interleave_
         return true;
     }
 
-    // Fast layout: decide the metadata kind for the whole fused matrix.
+    std::vector<uint8_t> host;
+    if (!build_matrix_rows(parts, interleave_pairs, out, &host, error)) return false;
+    return upload_matrix_rows(host, out, error);
+}
+
+bool build_matrix_rows(const std::vector<const HostMatrix*>& parts, bool interleave_pairs, DevMatrix* out,
+                       std::vector<uint8_t>* host_out, std::string* error) {
+    const int cols = parts[0]->cols, group = parts[0]->group;
+    int rows = 0;
+    for (const HostMatrix* p : parts) {
+        if (p->cols != cols || p->group != group) {
+            *error = "matrices fused into one launch must share cols and group size";
+            return false;
+        }
+        rows += p->rows;
+    }
+    if (!fast_shape(cols, group)) {
+        *error = "matrix shape has no fused row layout";
+        return false;
+    }
+    if (interleave_pairs && (parts.size() != 2 || parts[0]->rows != parts[1]->rows)) {
+        *error = "paired matrices must have equal rows";
+        return false;
+    }
+    const int gpr = (cols + group - 1) / group;
+    out->rows = rows;
+    out->cols = cols;
+    out->group = group;
+    out->version = parts[0]->version;
+    // Decide the metadata kind for the whole fused matrix.
     bool sym = true;
     for (const HostMatrix* p : parts) {
         if (p->version != 1) sym = false;
@@ -148,7 +177,8 @@ bool upload_matrix(const std::vector<const HostMatrix*>& parts, bool interleave_
     out->kind = sym ? 0 : 1;
     out->meta_offset = cols / 2;
     out->row_stride = cols / 2 + (sym ? 2 : 8) * gpr;  // multiple of 16 since cols % 1024 == 0
-    std::vector<uint8_t> host(static_cast<size_t>(rows) * out->row_stride);
+    std::vector<uint8_t>& host = *host_out;
+    host.assign(static_cast<size_t>(rows) * out->row_stride, 0);
     size_t dst_row = 0;
     auto emit = [&](const HostMatrix* p, int r) {
         uint8_t* d = host.data() + dst_row * out->row_stride;
@@ -177,9 +207,78 @@ bool upload_matrix(const std::vector<const HostMatrix*>& parts, bool interleave_
         for (const HostMatrix* p : parts)
             for (int r = 0; r < p->rows; ++r) emit(p, r);
     }
+    return true;
+}
+
+bool upload_matrix_rows(const std::vector<uint8_t>& host, DevMatrix* out, std::string* error) {
+    (void)error;
     out->bytes = host.size();
     XQB_CUDA_OK(cudaMalloc(&out->d_rows, host.size()));
     XQB_CUDA_OK(cudaMemcpy(out->d_rows, host.data(), host.size(), cudaMemcpyHostToDevice));
+    return true;
+}
+
+namespace {
+struct B200Header {
+    char magic[8];  // "XQB200\0\0"
+    uint32_t version, kind, rows, cols, group, xq4_version, row_stride, meta_offset;
+    uint64_t bytes;
+    uint8_t reserved[16];
+};
+static_assert(sizeof(B200Header) == 64, "packed header");
+constexpr char kB200Magic[8] = {'X', 'Q', 'B', '2', '0', '0', '\0', '\0'};
+}  // namespace
+
+bool write_b200_file(const std::string& path, const DevMatrix& m, const std::vector<uint8_t>& host,
+                     std::string* error) {
+    B200Header h = {};
+    std::memcpy(h.magic, kB200Magic, 8);
+    h.version = 1;
+    h.kind = static_cast<uint32_t>(m.kind);
+    h.rows = static_cast<uint32_t>(m.rows);
+    h.cols = static_cast<uint32_t>(m.cols);
+    h.group = static_cast<uint32_t>(m.group);
+    h.xq4_version = static_cast<uint32_t>(m.version);
+    h.row_stride = static_cast<uint32_t>(m.row_stride);
+    h.meta_offset = static_cast<uint32_t>(m.meta_offset);
+    h.bytes = host.size();
+    std::ofstream f(path, std::ios::binary | std::ios::trunc);
+    f.write(reinterpret_cast<const char*>(&h), sizeof h);
+    f.write(reinterpret_cast<const char*>(host.data()), static_cast<std::streamsize>(host.size()));
+    if (!f) {
+        *error = "cannot write " + path;
+        return false;
+    }
+    return true;
+}
+
+bool read_b200_file(const std::string& path, DevMatrix* m, std::vector<uint8_t>* host, std::string* error) {
+    std::ifstream f(path, std::ios::binary);
+    B200Header h;
+    if (!f.read(reinterpret_cast<char*>(&h), sizeof h) || std::memcmp(h.magic, kB200Magic, 8) != 0 || h.version != 1) {
+        *error = "not a packed B200 matrix: " + path;
+        return false;
+    }
+    const uint32_t gpr = h.group ? (h.cols + h.group - 1) / h.group : 0;
+    if (h.kind > 1 || !fast_shape(static_cast<int>(h.cols), static_cast<int>(h.group)) ||
+        h.meta_offset != h.cols / 2 || h.row_stride != h.cols / 2 + (h.kind == 0 ? 2u : 8u) * gpr ||
+        h.bytes != static_cast<uint64_t>(h.rows) * h.row_stride) {
+        *error = "inconsistent packed B200 header: " + path;
+        return false;
+    }
+    host->resize(h.bytes);
+    if (!f.read(reinterpret_cast<char*>(host->data()), static_cast<std::streamsize>(h.bytes))) {
+        *error = "truncated packed B200 matrix: " + path;
+        return false;
+    }
+    *m = DevMatrix();
+    m->rows = static_cast<int>(h.rows);
+    m->cols = static_cast<int>(h.cols);
+    m->group = static_cast<int>(h.group);
+    m->version = static_cast<int>(h.xq4_version);
+    m->kind = static_cast<int>(h.kind);
+    m->row_stride = static_cast<int>(h.row_stride);
+    m->meta_offset = static_cast<int>(h.meta_offset);
     return true;
 }
 

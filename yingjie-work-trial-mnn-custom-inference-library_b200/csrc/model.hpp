@@ -45,6 +45,11 @@ struct DevLayer {
     void* v_cache = nullptr;
 };
 
+// Write the fused weight matrices of the package in `dir` in the device row layout to
+// dir/b200/*.b200 plus dir/b200/layout.json (host only, no GPU needed); the loader then reads
+// them instead of re-tiling the xq4 files.
+bool pack_b200_layout(const std::string& dir, std::string* error);
+
 struct Options {
     int device = 0;
     bool kv_fp16 = false;
@@ -95,6 +100,7 @@ public:
     int kernels_per_decode_step() const;
     int kernels_per_prefill_step() const;
     bool persistent() const { return persistent_; }
+    bool packed_layout() const { return packed_layout_; }
     cudaStream_t stream() const { return stream_; }
     const std::vector<DevLayer>& layers() const { return layers_; }
     const DevMatrix& lm_head() const { return lm_head_; }
@@ -160,6 +166,7 @@ private:
     int step_l2_ahead_ = 0;  // chunks (XQ_STEP_L2_AHEAD); prefetching into L2 measured slower
     PhaseDesc* d_phases_decode_ = nullptr;
     void* d_tmaps_ = nullptr;  // CUtensorMap array of the phase lists
+    bool packed_layout_ = false;  // weights read from b200/*.b200
     unsigned long long* d_block_done_ = nullptr;  // XQ_STEP_TRACE >= 2: per-block phase finish times
     std::vector<double> block_late_ns_;
     std::vector<double> barrier_ns_;
