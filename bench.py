@@ -191,6 +191,24 @@ def cpu_baseline(model_dir, steps):
                       f"package; the reference's WorkerPool caps at min(8, hardware_concurrency) threads"}
 
 
+def max_over_ranks(x: float, world: int, device: str = "cuda") -> float:
+    """The largest per-rank value of x (a rank's timed duration): every rank takes the same
+    collective steps; with world == 1 it is x itself."""
+    if world <= 1:
+        return float(x)
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([float(x)], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_rate(units_per_rank: int, world: int, seconds_max: float) -> float:
+    """Whole-job throughput of replicas: all ranks' units over the slowest rank's time."""
+    return world * units_per_rank / seconds_max
+
+
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return 0
@@ -259,12 +277,10 @@ def main():
         torch.cuda.synchronize()
         dev_ms, toks = sess.decode_timed(args.steps, want_tokens=True)
         torch.cuda.synchronize()
-    t = torch.tensor([dev_ms], device="cuda", dtype=torch.float64)
     if world > 1:
         dist.barrier()
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    value = world * args.steps / (ms_max / 1000.0)
+    ms_max = max_over_ranks(dev_ms, world)
+    value = job_rate(args.steps, world, ms_max / 1000.0)
 
     # e2e: the same metric through xq_decode_one (host API call; 4-byte token read back per step)
     e2e_steps = min(args.steps, 64)
@@ -272,10 +288,7 @@ def main():
     for _ in range(e2e_steps):
         sess.decode_one()
     e2e_s = time.perf_counter() - t0
-    te = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * e2e_steps / float(te.item())
+    e2e_value = job_rate(e2e_steps, world, max_over_ranks(e2e_s, world))
 
     info = json.loads(sess.json("backend"))
     if os.environ.get("XQ_STEP_TRACE") and rank == 0 and info.get("step_phase_trace"):
