@@ -40,6 +40,14 @@ XQK_API int xqk_matrix_info(const xqk_matrix* m, int* rows, int* cols, size_t* d
 
 /* y = W x, fp32 in/out, device pointers (gemvW4A16Neon, xq_gemv_w4a16_neon.cpp:259). */
 XQK_API int xqk_gemv_w4a16(const xqk_matrix* m, const float* x_dev, float* y_dev, void* stream);
+/* y = W x on the integer tensor cores (mma.sync m16n8k32, u8 weight codes x s8 digits of x,
+ * exact s32 sums, group scale applied once per row and group). No reference counterpart: the
+ * same mathematics as xqk_gemv_w4a16 with x held per 64-column group instead of per 32
+ * columns, so results agree with it to fp32 rounding, not bit for bit. Served for symmetric
+ * version-1 matrices (zero 8) with group 64, fp16-exact scales, cols a multiple of 512 (and
+ * of 4096 above 4096), which xqk_matrix_create then also stores in the tensor-core tile
+ * layout; other matrices return XQ_ERR_NOT_READY (-2). Finite x only. */
+XQK_API int xqk_gemv_w4a16_mma(const xqk_matrix* m, const float* x_dev, float* y_dev, void* stream);
 /* Same with host buffers: copies x in, runs, copies y out, synchronises. */
 XQK_API int xqk_gemv_w4a16_host(const xqk_matrix* m, const float* x_host, float* y_host);
 /* argmax_r (W x)[r], ties to the lowest index (gemvW4A16ArgmaxNeon,

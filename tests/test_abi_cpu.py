@@ -35,6 +35,18 @@ def test_exports_every_declared_symbol():
         assert hasattr(L, n), n
 
 
+def test_binding_declares_every_argument_list():
+    """ctypes passes an undeclared pointer argument as a 32-bit int: every entry point that
+    takes arguments must have its argtypes set by the Python binding."""
+    L = PKG.lib()
+    for h in ("xqwen35.h", "xq_kernels.h"):
+        with open(os.path.join(ROOT, "include", h)) as f:
+            src = f.read()
+        for name, args in re.findall(r"XQK?_API\s+[\w\s\*]+?\b(\w+)\s*\(([^)]*)\)", src):
+            if args.strip() not in ("", "void"):
+                assert getattr(L, name).argtypes is not None, name
+
+
 def test_null_arguments_follow_reference_status_codes():
     L = PKG.lib()
     out = C.c_void_p()

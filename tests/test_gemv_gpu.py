@@ -117,3 +117,35 @@ def test_nan_input_propagates():
     x[17] = np.nan
     m = PKG.Matrix(packed, s, z, 256, 4096, 64)
     assert np.isnan(run_gemv(m, x)).all()
+
+
+def run_gemv_mma(m, x):
+    torch = _torch()
+    xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    yd = torch.full((m.rows,), float("nan"), dtype=torch.float32, device="cuda")
+    m.gemv_mma(xd.data_ptr(), yd.data_ptr())
+    torch.cuda.synchronize()
+    return yd.cpu().numpy()
+
+
+@pytest.mark.parametrize("rows,cols", [(24576, 4096), (4096, 12288), (1000, 4096), (7, 512), (333, 1024)])
+def test_tensor_core_gemv_vs_oracle(oracle, rows, cols):
+    """The mma.sync tile-layout GEMV: every row written (ragged last tile), within the fp32 bar."""
+    packed, s, z, version, x = seeded(rows, cols, "sym", seed=rows + 5)
+    x[::7] *= 1e-3  # small and large values in one group
+    m = PKG.Matrix(packed, s, z, rows, cols, 64, version)
+    ref = oracle.port_gemv(oracle.Matrix(rows, cols, 64, version, packed, s, z), x)
+    y = run_gemv_mma(m, x)
+    assert np.all(np.isfinite(y))
+    assert rel_err(y, ref) <= TOL
+    assert rel_err(y, run_gemv(m, x)) <= TOL
+
+
+def test_tensor_core_gemv_refuses_other_layouts():
+    packed, s, z, version, x = seeded(64, 4096, "asym", seed=3)
+    m = PKG.Matrix(packed, s, z, 64, 4096, 64, version)
+    torch = _torch()
+    xd = torch.zeros(4096, device="cuda")
+    yd = torch.zeros(64, device="cuda")
+    with pytest.raises(RuntimeError):
+        m.gemv_mma(xd.data_ptr(), yd.data_ptr())

@@ -11,6 +11,7 @@
 
 #include "../../include/xq_kernels.h"
 #include "gemv.hpp"
+#include "mma_gemv.hpp"
 
 namespace xqb {
 
@@ -503,6 +504,7 @@ struct xqk_matrix {
     unsigned* err = nullptr;
     float* y_tmp = nullptr;  // generic argmax / host path staging
     float* x_tmp = nullptr;
+    xqb::MmaMatrix mma;  // tensor-core tile copy, when the layout serves the matrix
 };
 
 namespace {
@@ -513,7 +515,7 @@ bool ensure_device(int device) {
     std::lock_guard<std::mutex> lock(g_init_mu);
     XQB_CUDA_OK(cudaSetDevice(device));
     if (device >= 0 && device < 64 && !g_inited[device]) {
-        if (!xqb::gemv_init_device()) return false;
+        if (!xqb::gemv_init_device() || !xqb::mma_init_device()) return false;
         g_inited[device] = true;
     }
     return true;
@@ -551,6 +553,11 @@ int xqk_matrix_create(const uint8_t* packed, const float* scales, const float* z
         delete m;
         return -3;
     }
+    if (xqb::mma_eligible(h) && !xqb::build_mma_matrix(h, &m->mma, &err)) {
+        xqb::set_last_error(err.empty() ? xqb::last_error() : err);
+        xqk_matrix_destroy(m);
+        return -4;
+    }
     const int nb = m->num_sms;
     if (cudaMalloc(&m->part_val, nb * sizeof(float)) != cudaSuccess ||
         cudaMalloc(&m->part_idx, nb * sizeof(int)) != cudaSuccess ||
@@ -572,6 +579,7 @@ void xqk_matrix_destroy(xqk_matrix* m) {
     if (!m) return;
     cudaSetDevice(m->device);
     xqb::free_matrix(&m->m);
+    xqb::free_mma_matrix(&m->mma);
     cudaFree(m->part_val);
     cudaFree(m->part_idx);
     cudaFree(m->counter);
@@ -606,6 +614,17 @@ int xqk_gemv_w4a16(const xqk_matrix* m, const float* x_dev, float* y_dev, void* 
     ctx.num_sms = m->num_sms;
     ctx.pdl = false;
     return xqb::launch_gemv(m->m, xqb::kProPlain, xqb::kEpiStore, p, 1, ctx) ? 0 : -4;
+}
+
+int xqk_gemv_w4a16_mma(const xqk_matrix* m, const float* x_dev, float* y_dev, void* stream) {
+    if (!m || !x_dev || !y_dev) return -1;
+    if (!m->mma.d_tiles) {
+        xqb::set_last_error("xqk_gemv_w4a16_mma: matrix not in the tensor-core layout (needs symmetric xq4 v1, "
+                            "group 64, fp16-exact scales, cols a multiple of 512 and of 4096 above 4096)");
+        return -2;
+    }
+    return xqb::launch_mma_gemv(m->mma, x_dev, y_dev, m->err, m->num_sms, static_cast<cudaStream_t>(stream)) ? 0
+                                                                                                              : -4;
 }
 
 int xqk_gemv_w4a16_host(const xqk_matrix* m, const float* x_host, float* y_host) {
