@@ -152,6 +152,16 @@ __device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) 
         if (global_ns() - t0 > kWaitLimitNs) return;
 }
 
+// d += A B on the integer tensor cores: mma.sync m16n8k32, A unsigned 8-bit (row-major
+// fragment a0..a3), B signed 8-bit (column-major fragment b0, b1), exact s32 accumulation. Not
+// volatile: the compiler may interleave independent accumulator chains.
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
     int d;
     asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));

@@ -288,6 +288,7 @@ void free_matrix(DevMatrix* m) {
     cudaFree(m->d_packed);
     cudaFree(m->d_scales);
     cudaFree(m->d_zeros);
+    cudaFree(m->d_tiles);
     *m = DevMatrix();
 }
 

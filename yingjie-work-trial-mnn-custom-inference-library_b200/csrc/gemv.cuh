@@ -24,7 +24,8 @@
 
 namespace xqb {
 
-enum MetaKind : int { kMetaSym16 = 0, kMetaAff32 = 1 };
+// kMetaMma: the symmetric layout's 16-row tensor-core tiles (mma_gemv.hpp), step kernel only.
+enum MetaKind : int { kMetaSym16 = 0, kMetaAff32 = 1, kMetaMma = 2 };
 enum Prologue : int { kProPlain = 0, kProRms = 1, kProGatedRms = 2 };
 enum Epilogue : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiglu = 2, kEpiConv = 3, kEpiArgmax = 4 };
 
@@ -44,6 +45,9 @@ struct GemvParams {
     int stages;          // depth of the shared-memory ring, <= kMaxStages
     int unit;            // CTA row ranges are multiples of this (2 for gate/up pairs)
     int evict_first;     // stream the rows with the L2 evict-first policy
+    // Tensor-core tiles (w points at them when mma_pairs > 0): 128-column pairs per 16-row tile,
+    // and pairs per streamed chunk (a divisor of mma_pairs, a multiple of 4).
+    int mma_pairs, mma_ppc;
     // prologue
     const float* x;
     const float* norm_w;  // kProRms: [cols]; kProGatedRms: [head_dim]

@@ -32,6 +32,8 @@ struct DevMatrix {
     float* d_scales = nullptr;
     float* d_zeros = nullptr;
     size_t bytes = 0;
+    uint8_t* d_tiles = nullptr;  // optional 16-row tensor-core tile copy (symmetric layout)
+    size_t tile_bytes = 0;
     bool fast() const { return kind != 2; }
 };
 

@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 #include "gemv.hpp"
 
@@ -12,6 +13,8 @@ namespace xqb {
 
 // A matrix in the "mma16" tile layout: 16-row tiles, per tile and pair of 64-column groups
 // 1088 bytes (four 32-column slabs of fragment-ordered nibbles, then fp16 scales).
+constexpr int kMmaUnitBytes = 1088;  // one 16-row tile x one pair of groups (128 columns)
+
 struct MmaMatrix {
     int rows = 0, cols = 0, ntiles = 0, pairs = 0;
     size_t bytes = 0;
@@ -23,6 +26,9 @@ struct MmaMatrix {
 bool mma_eligible(const HostMatrix& h);
 bool build_mma_matrix(const HostMatrix& h, MmaMatrix* out, std::string* error);
 void free_mma_matrix(MmaMatrix* m);
+// Build the tile copy of a symmetric row-layout matrix from its host rows (as
+// build_matrix_rows / read_b200_file give them) into m->d_tiles.
+bool attach_mma_tiles(const std::vector<uint8_t>& rows_host, DevMatrix* m, std::string* error);
 bool mma_init_device();
 // y = W x (fp32 in/out, device pointers); one block per SM, at most num_sms blocks.
 bool launch_mma_gemv(const MmaMatrix& m, const float* x, float* y, unsigned* err, int num_sms, cudaStream_t s);
