@@ -321,7 +321,9 @@ def main():
                        "kv_dtype": "f16" if args.kv_fp16 else "f32", "parallelism": f"replicas{world}",
                        "l2": "inputs larger than L2 (4.3 GB of weights streamed per step)",
                        "step_execution": "persistent cooperative kernel" if info.get("persistent_step_kernel")
-                       else "CUDA graph of per-op kernels with PDL"},
+                       else "CUDA graph of per-op kernels with PDL",
+                       "step_gemv": "integer tensor cores (mma.sync m16n8k32 u8 x s8, exact s32)"
+                       if info.get("tensor_core_gemv") else "dp4a"},
             "prefill_tok_s": round(prefill_tok_s, 2),
             "roofline": dict(roof, peak_kind=peak_kind),
             "gemv_kernel": dict(gemv, peak_kind=peak_kind) if gemv else None,

@@ -475,7 +475,13 @@ bool DeviceModel::load(const std::string& dir, const Options& opts, std::string*
             tiles = tiles && L.in_proj.d_tiles && L.out_proj.d_tiles && L.gate_up.d_tiles && L.down.d_tiles;
         if (persistent_ && tiles) meta_kind_ = kMetaMma;
         if (persistent_) {
-            step_slot_bytes_ = meta_kind_ == kMetaMma ? kMmaStepSlotBytes : kStepSlotBytes;
+            step_slot_bytes_ = kStepSlotBytes;
+            if (meta_kind_ == kMetaMma) {
+                // pairs of groups per ring slot (XQ_STEP_MMA_PAIRS: 8..32, a multiple of 8)
+                int pairs = kMmaStepSlotBytes / kMmaUnitBytes;
+                if (const char* v = std::getenv("XQ_STEP_MMA_PAIRS")) pairs = std::max(8, std::min(32, std::atoi(v))) & ~7;
+                step_slot_bytes_ = pairs * kMmaUnitBytes;
+            }
             step_slots_ = step_max_slots(step_slot_bytes_);
             step_inflight_ = step_slots_;
             if (const char* v = std::getenv("XQ_STEP_INFLIGHT")) step_inflight_ = std::atoi(v);
@@ -598,12 +604,12 @@ bool DeviceModel::build_phases(std::string* error) {
         g.meta_offset = m.meta_offset;
         g.rows_per_chunk = kStepSlotBytes / m.row_stride >= 8 ? 8 : 4;
         if (meta_kind_ == kMetaMma) {
-            // chunks of up to 16 pairs (17408 bytes, one ring slot), a multiple of 4 (one per warp
-            // of a team) that divides the tile's pairs
+            // chunks of up to one ring slot of pairs (16 by default), a multiple of 8 (an even
+            // number per warp of a team) that divides the tile's pairs
             g.w = m.d_tiles;
             g.mma_pairs = m.cols / 128;
             g.mma_ppc = 0;
-            for (int k = 4; k * kMmaUnitBytes <= kMmaStepSlotBytes; k += 4)
+            for (int k = 8; k * kMmaUnitBytes <= step_slot_bytes_; k += 8)
                 if (g.mma_pairs % k == 0) g.mma_ppc = k;
             if (g.mma_ppc == 0) staged_ok = false;
         }
@@ -998,7 +1004,7 @@ bool DeviceModel::run_step(bool decode, std::string* error) {
                 phase_ns_[S * ph] += start - prev_end;  // barrier latency
                 for (int k = 1; k < S; ++k) {
                     if (!t[S * ph + k]) continue;
-                    if (k >= 8)
+                    if (k == 8 || k == 9)
                         phase_ns_[S * ph + k] += static_cast<double>(t[S * ph + k]);  // durations
                     else
                         phase_ns_[S * ph + k] += static_cast<double>(t[S * ph + k]) - start;
@@ -1371,7 +1377,7 @@ std::string DeviceModel::phase_trace_summary() const {
     // Per slot: the summed microseconds of all phases of that name, per step.
     static const char* kSlotNames[S] = {"barrier_us",    "block0_us",     "last_arrival_us", "x_loaded_us",
                                         "limbs_ready_us", "first_chunk_us", "loop_done_us",   "constants_staged_us",
-                                        "chunk_wait_us", "producer_slot_wait_us"};
+                                        "chunk_wait_us", "producer_slot_wait_us", "x_staged_us"};
     std::ostringstream o;
     o << "{\"steps\":" << traced_steps_ << ",\"phases\":[";
     bool first = true;

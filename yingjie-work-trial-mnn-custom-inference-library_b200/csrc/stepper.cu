@@ -29,7 +29,7 @@ constexpr int kOffFull = 0, kOffEmpty = 128, kOffWsum = 256, kOffXBar = 384, kOf
 constexpr int kDescBytes = 512;
 constexpr int kMmaStepTeams = 3, kMmaStepWarpsPerTeam = 4;  // tensor-core phases: 12 consumer warps
 static_assert(kMmaStepTeams * kMmaStepWarpsPerTeam * 32 == kStepConsumers, "tensor-core teams");
-static_assert(kMmaStepSlotBytes == 16 * kMmaUnitBytes, "tensor-core ring slot");
+static_assert(kMmaStepSlotBytes % kMmaUnitBytes == 0, "tensor-core ring slot");
 constexpr int kOffAct = 10240;  // 1024-byte aligned: 128-byte swizzled tensor copies land here
 constexpr int kOffEpi = kOffAct + kStepActBytes;
 constexpr int kOffRing = kOffEpi + 4 * kStepEpiFloats;
@@ -491,6 +491,7 @@ __device__ __forceinline__ void gemv_phase(const GemvParams& p, const int pro, c
     mbar_wait_bounded(c.cbar, c.parity, p.err);
     if (ts && tid == 0) ts[7] = global_ns();
     mbar_wait_bounded(c.xbar, c.parity, p.err);
+    if (ts && tid == 0) ts[10] = global_ns();
     if (pro == kProGatedRms) gated_prologue(p, c);
     if (tid < teams * team_size) {
         const int team = tid / team_size;
@@ -670,6 +671,7 @@ __device__ __forceinline__ void gemv_phase_mma(const GemvParams& p, const int pr
     mbar_wait_bounded(c.cbar, c.parity, p.err);
     if (ts && tid == 0) ts[7] = global_ns();
     mbar_wait_bounded(c.xbar, c.parity, p.err);
+    if (ts && tid == 0) ts[10] = global_ns();
     if (pro == kProGatedRms) gated_prologue(p, c);
     XDigits X;
     if (tid < nth) {
@@ -716,7 +718,7 @@ __device__ __forceinline__ void gemv_phase_mma(const GemvParams& p, const int pr
                 mbar_wait_bounded(&c.full[s], par, p.err);
             }
             const uint8_t* base = c.ring + static_cast<size_t>(s) * c.slot_bytes;
-            // two pairs per iteration (pw is 2 or 4): two independent accumulator chains
+            // two pairs per iteration (pw is even): two independent accumulator chains
             for (int k = 0; k < pw; k += 2) {
                 const int pl = wt * pw + k, pg = cc * ppc + pl;
                 const uint8_t* pb = base + pl * kMmaUnitBytes;
@@ -806,7 +808,9 @@ __device__ __forceinline__ void gemv_dispatch(const PhaseDesc& D, Ctx& c, unsign
                                            epi == kEpiArgmax)) ||
                        (pro == kProGatedRms && epi == kEpiResidual) || (pro == kProPlain && epi == kEpiResidual);
     if constexpr (META == kMetaMma) {
-        if (known && D.g.mma_pairs > 0 && D.g.cols >> 5 <= kStepConsumers)
+        if (known && D.g.mma_pairs > 0 && D.g.mma_ppc > 0 && D.g.mma_ppc % 8 == 0 &&
+            D.g.mma_pairs % D.g.mma_ppc == 0 && D.g.mma_ppc * kMmaUnitBytes <= c.slot_bytes &&
+            D.g.cols >> 5 <= kStepConsumers)
             gemv_phase_mma(D.g, pro, epi, c, ts);
         else if (c.tid == 0)
             atomicOr(D.g.err, kErrBadShape);
@@ -1056,10 +1060,10 @@ cudaError_t launch_one(const StepParams& p, int num_sms, cudaStream_t s) {
 
 template <int META, typename KV>
 cudaError_t set_attr() {
-    return cudaFuncSetAttribute(decode_step_kernel<META, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(std::max(
-                                    step_smem_bytes(step_max_slots(kStepSlotBytes), kStepSlotBytes),
-                                    step_smem_bytes(step_max_slots(kMmaStepSlotBytes), kMmaStepSlotBytes))));
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    return cudaFuncSetAttribute(decode_step_kernel<META, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
 }
 
 }  // namespace
