@@ -263,6 +263,10 @@ __device__ __forceinline__ void attention_item(const AttnParams& p, int kh, int 
         // Merge the splits in parallel: (max, sum) of every (split, head) pair to shared memory,
         // one rescale weight per pair, then thread d sums its dimension over the splits.
         const float* base = p.part + static_cast<size_t>(kh * kAttnSplits) * group * (hd + 2);
+        float gate[kAttnMaxGroup];  // output gates, loaded with the (max, sum) pairs
+#pragma unroll
+        for (int g = 0; g < kAttnMaxGroup; ++g)
+            gate[g] = g < group ? __ldcg(p.qkv + static_cast<size_t>(kh * group + g) * 2 * hd + hd + tid) : 0.0f;
         if (tid < kAttnSplits * group) {
             const float* ps = base + tid * (hd + 2);  // tid = split * group + g
             sh->pm[tid] = __ldcg(ps + hd);
@@ -280,19 +284,17 @@ __device__ __forceinline__ void attention_item(const AttnParams& p, int kh, int 
         bar_sync(bar_id, kAttnThreads);
         if (tid < kAttnSplits * group) sh->pm[tid] = expf(sh->pm[tid] - sh->M[tid % group]);
         bar_sync(bar_id, kAttnThreads);
-        for (int g = 0; g < group; ++g) {
+#pragma unroll
+        for (int g = 0; g < kAttnMaxGroup; ++g) {
+            if (g >= group) break;
+            float part[kAttnSplits];  // every split of this head in flight in one round trip
+#pragma unroll
+            for (int u = 0; u < kAttnSplits; ++u) part[u] = __ldcg(base + (u * group + g) * (hd + 2) + tid);
             float O = 0.0f;
 #pragma unroll
-            for (int h = 0; h < kAttnSplits; h += 16) {  // 16 requests in flight per round trip
-                float part[16];
-#pragma unroll
-                for (int u = 0; u < 16; ++u) part[u] = __ldcg(base + ((h + u) * group + g) * (hd + 2) + tid);
-#pragma unroll
-                for (int u = 0; u < 16; ++u) O += part[u] * sh->pm[(h + u) * group + g];
-            }
+            for (int u = 0; u < kAttnSplits; ++u) O += part[u] * sh->pm[u * group + g];
             const int qh = kh * group + g;
-            const float gate = __ldcg(p.qkv + static_cast<size_t>(qh) * 2 * hd + hd + tid);
-            p.out[qh * hd + tid] = (O * sh->invL[g]) * dsigmoid(gate);  // output gate, custom_model.cpp:944-946
+            p.out[qh * hd + tid] = (O * sh->invL[g]) * dsigmoid(gate[g]);  // output gate, custom_model.cpp:944-946
         }
         if (tid == 0) p.counters[kh] = 0u;
     }
