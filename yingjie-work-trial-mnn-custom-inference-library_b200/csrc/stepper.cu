@@ -149,47 +149,62 @@ __device__ __forceinline__ void tma_vector(float* dst, const void* tmap, int n, 
             : "memory");
 }
 
-// Constant inputs of a GEMV phase (norm weights, conv weights, this block's conv state, which
-// only this block writes, in an earlier launch): issued before the grid barrier that opens the
-// phase. Always arms cbar once.
+__device__ __forceinline__ void prefetch_tensormap(const void* tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// Inputs of a GEMV phase that do not depend on the phase just before it, issued by thread 0
+// right after this block arrives at the grid barrier that closes that phase: norm weights, conv
+// weights and this block's conv state (which only this block writes), the gate of a gated
+// prologue (written by the in_proj two phases earlier) and this block's residual rows (the
+// hidden state, last written two or more phases earlier and not written by the phase in
+// between). This block passed the barrier that closed those writers' phase, and this thread
+// acquired it; the proxy fence orders those writes before the bulk copies. Also warms the
+// descriptor of x's tensor map. Always arms cbar once.
 __device__ __forceinline__ void issue_constants(const PhaseDesc& D, Ctx& c) {
-    fence_proxy_async_smem();  // the area was last read by generic loads
+    fence_proxy_async_smem();  // the areas were last read by generic loads
+    fence_proxy_async_global();
     uint32_t bytes = 0;
     const void* src[3] = {nullptr, nullptr, nullptr};
     void* dst[3] = {nullptr, nullptr, nullptr};
     uint32_t len[3] = {0, 0, 0};
-    int vec_n = 0, vec_map = 0;
+    int vec_n = 0, vec_map = 0, gate_n = 0;
     float* vec_dst = nullptr;
     if (D.kind == kPhaseGemv) {
         const GemvParams& p = D.g;
+        prefetch_tensormap(D.tmap[0]);
         if (D.pro == kProRms) {
             vec_n = p.cols, vec_map = 1, vec_dst = c.act + p.cols;
         } else if (D.pro == kProGatedRms) {
             vec_n = p.head_dim, vec_map = 2, vec_dst = c.act + 2 * p.cols;
+            gate_n = p.cols;
         }
+        int r_begin, r_end, nchunks;
+        block_rows(p, &r_begin, &r_end, &nchunks);
         if (D.epi == kEpiConv) {
-            int r_begin, r_end, nchunks;
-            block_rows(p, &r_begin, &r_end, &nchunks);
             const EpiWindow w = epi_window(p, kEpiConv, r_begin, r_end);
             if (w.ok) {
                 const int n = w.r1 - w.r0;
                 src[1] = p.conv_w + static_cast<size_t>(w.r0) * 4, dst[1] = c.epi, len[1] = 16u * n;
                 src[2] = p.conv_state + static_cast<size_t>(w.r0) * 3, dst[2] = c.epi + 4 * n, len[2] = 12u * n;
             }
+        } else if (D.epi == kEpiResidual) {
+            const EpiWindow w = epi_window(p, kEpiResidual, r_begin, r_end);
+            if (w.ok) src[0] = p.out + w.r0, dst[0] = c.epi, len[0] = 4u * (w.r1 - w.r0);
         }
     }
     for (int k = 0; k < 3; ++k) bytes += len[k];
-    mbar_expect_tx(c.cbar, bytes + 4u * vec_n);
+    mbar_expect_tx(c.cbar, bytes + 4u * (vec_n + gate_n));
     if (vec_n) tma_vector(vec_dst, D.tmap[vec_map], vec_n, c.cbar);
+    if (gate_n) tma_vector(c.act + D.g.cols, D.tmap[1], gate_n, c.cbar);
     for (int k = 0; k < 3; ++k)
         if (len[k]) bulk_g2s(dst[k], src[k], len[k], c.cbar);
 }
 
-// Activation inputs of a GEMV phase (x, the gate of a gated prologue, this block's residual
-// rows): issued right after the grid barrier, whose acquire makes the other blocks' stores
-// visible; the proxy fence extends that to the bulk copies. Always arms xbar once.
-// Called by all 32 lanes of warp 0: lane 0 arms xbar with the total byte count, then the lanes
-// issue the tensor-copy boxes in parallel (a 48 KB x is 12 boxes).
+// x of a GEMV phase (the previous phase's output): issued right after the grid barrier that
+// opens the phase, whose acquire makes the other blocks' stores visible; the proxy fence extends
+// that to the tensor copies. Always arms xbar once. Called by all 32 lanes of warp 0: lane 0
+// arms xbar, then lanes 0-15 issue the boxes in parallel (a 48 KB x is 12 boxes).
 __device__ __forceinline__ void issue_activations(const PhaseDesc& D, Ctx& c, int lane) {
     fence_proxy_async_global();
     fence_proxy_async_smem();
@@ -198,23 +213,9 @@ __device__ __forceinline__ void issue_activations(const PhaseDesc& D, Ctx& c, in
         return;
     }
     const GemvParams& p = D.g;
-    const bool gated = D.pro == kProGatedRms;
-    const void* rsrc = nullptr;
-    uint32_t rlen = 0;
-    if (D.epi == kEpiResidual) {
-        int r_begin, r_end, nchunks;
-        block_rows(p, &r_begin, &r_end, &nchunks);
-        const EpiWindow w = epi_window(p, kEpiResidual, r_begin, r_end);
-        if (w.ok) rsrc = p.out + w.r0, rlen = 4u * (w.r1 - w.r0);
-    }
-    if (lane == 0) mbar_expect_tx(c.xbar, 4u * p.cols * (gated ? 2u : 1u) + rlen);
+    if (lane == 0) mbar_expect_tx(c.xbar, 4u * p.cols);
     __syncwarp();
-    // lanes 0-15: boxes of x; lanes 16-31: boxes of the gate (n / 32 <= 512 rows: <= 16 boxes each)
-    if (lane < 16)
-        tma_vector(c.act, D.tmap[0], p.cols, c.xbar, lane, 16);
-    else if (gated)
-        tma_vector(c.act + p.cols, D.tmap[1], p.cols, c.xbar, lane - 16, 16);
-    if (rlen && lane == 31) bulk_g2s(c.epi, rsrc, rlen, c.xbar);
+    if (lane < 16) tma_vector(c.act, D.tmap[0], p.cols, c.xbar, lane, 16);
 }
 
 // One output row's epilogue with its inputs from the staging area when `w.ok`.
@@ -974,6 +975,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) decode_step_kernel(const Step
             }
             __syncwarp();
             issue_activations(desc[ph & 1], c, c.lane);  // descriptor waited for at the end of phase ph - 1
+            if (P.trace && blockIdx.x == 0 && c.lane == 0) P.trace[kStepTraceSlots * ph + 12] = global_ns();
         }
         named_bar(1, kStepConsumers);
         wait_desc(ph);
