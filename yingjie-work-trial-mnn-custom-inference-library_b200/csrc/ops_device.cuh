@@ -197,19 +197,30 @@ __device__ __forceinline__ void attention_item(const AttnParams& p, int kh, int 
     }
     bar_sync(bar_id, kAttnThreads);
 
-    // scores s = q . k / sqrt(hd) (custom_model.cpp:871-885)
+    // scores s = q . k / sqrt(hd) (custom_model.cpp:871-885); warp w takes positions t0 + w,
+    // t0 + w + 8, ..., loading three of its K rows per memory round trip
     const float rs = sqrtf(static_cast<float>(hd));
-    for (int t = t0 + warp; t < t1; t += kAttnThreads / 32) {
-        const KV* kr = kc + (static_cast<size_t>(t) * p.nkv + kh) * hd;
-        float kv[8];
+    constexpr int kNW = kAttnThreads / 32;
+    for (int tb = t0 + warp; tb < t1; tb += 3 * kNW) {
+        float kv[3][8];
 #pragma unroll
-        for (int m = 0; m < 8; ++m) kv[m] = kv_ld(kr + lane + 32 * m);
-        for (int g = 0; g < group; ++g) {
-            float d = 0.0f;
+        for (int u = 0; u < 3; ++u) {
+            const int t = tb + u * kNW;
+            const KV* kr = kc + (static_cast<size_t>(min(t, t1 - 1)) * p.nkv + kh) * hd;
 #pragma unroll
-            for (int m = 0; m < 8; ++m) d += qs[g * hd + lane + 32 * m] * kv[m];
-            d = warp_sum(d);
-            if (lane == 0) sc[g * cmax + (t - t0)] = d / rs;
+            for (int m = 0; m < 8; ++m) kv[u][m] = t < t1 ? kv_ld(kr + lane + 32 * m) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 3; ++u) {
+            const int t = tb + u * kNW;
+            if (t >= t1) break;
+            for (int g = 0; g < group; ++g) {
+                float d = 0.0f;
+#pragma unroll
+                for (int m = 0; m < 8; ++m) d += qs[g * hd + lane + 32 * m] * kv[u][m];
+                d = warp_sum(d);
+                if (lane == 0) sc[g * cmax + (t - t0)] = d / rs;
+            }
         }
     }
     bar_sync(bar_id, kAttnThreads);
@@ -233,13 +244,13 @@ __device__ __forceinline__ void attention_item(const AttnParams& p, int kh, int 
     float o[kAttnMaxGroup];
 #pragma unroll
     for (int g = 0; g < kAttnMaxGroup; ++g) o[g] = 0.0f;
-    for (int j0 = 0; j0 < n; j0 += 8) {  // V reduction (custom_model.cpp:910-928), thread = dim
-        float vb[8];                       // 8 requests in flight per round trip
+    for (int j0 = 0; j0 < n; j0 += 24) {  // V reduction (custom_model.cpp:910-928), thread = dim
+        float vb[24];                       // 24 requests in flight per round trip
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
+        for (int u = 0; u < 24; ++u)
             vb[u] = j0 + u < n ? kv_ld(vc + (static_cast<size_t>(t0 + j0 + u) * p.nkv + kh) * hd + tid) : 0.0f;
 #pragma unroll
-        for (int u = 0; u < 8; ++u)
+        for (int u = 0; u < 24; ++u)
             if (j0 + u < n) {
 #pragma unroll
                 for (int g = 0; g < kAttnMaxGroup; ++g)

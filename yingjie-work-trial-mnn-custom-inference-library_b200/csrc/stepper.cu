@@ -591,19 +591,22 @@ __device__ __forceinline__ float* mma_wtab(uint8_t* act, int K) {
     return reinterpret_cast<float*>(act + 3 * mma_digit_stride(K)) + K / 16;
 }
 
-// Digits of thread t's 32 columns (one half of group t / 2; the pair of lanes t, t ^ 1 shares
-// the group's exponent and digit sums).
+// Digits of thread t's E columns (E = 16 or 32; the 64 / E consecutive lanes of one 64-column
+// group share the group's exponent and digit sums).
+template <int E>
 struct XDigits {
-    uint32_t w[3][8];  // digit d of columns 4k .. 4k + 3 (byte j = column 4k + j)
-    int zs[3];         // digit sums of the whole group
+    uint32_t w[3][E / 4];  // digit d of columns 4k .. 4k + 3 (byte j = column 4k + j)
+    int zs[3];             // digit sums of the whole group
     int S;
     bool finite;
 };
-__device__ __forceinline__ void mma_make_digits(const float (&xv)[32], XDigits& X) {
+template <int E>
+__device__ __forceinline__ void mma_make_digits(const float (&xv)[E], XDigits<E>& X) {
     float amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(xv[i]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(xv[i]));
+#pragma unroll
+    for (int o = 1; o < 64 / E; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     X.finite = isfinite(amax);
     // As gemv_make_limbs: amax = f * 2^ex, f in [0.5, 1); m = round_to_nearest_even(x * 2^S)
     // with |m| < 2^22 sits in the low bits of x * 2^S + 1.5 * 2^23, and m + 0x808080 has the
@@ -613,7 +616,7 @@ __device__ __forceinline__ void mma_make_digits(const float (&xv)[32], XDigits& 
     const float up = __int_as_float((X.S + 127) << 23);
     int z0 = 0, z1 = 0, z2 = 0;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < E / 4; ++k) {
         uint32_t u[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j)
@@ -628,19 +631,28 @@ __device__ __forceinline__ void mma_make_digits(const float (&xv)[32], XDigits& 
         z1 = __dp4a(static_cast<int>(X.w[1][k]), 0x01010101, z1);
         z2 = __dp4a(static_cast<int>(X.w[2][k]), 0x01010101, z2);
     }
-    X.zs[0] = z0 + __shfl_xor_sync(0xffffffffu, z0, 1);
-    X.zs[1] = z1 + __shfl_xor_sync(0xffffffffu, z1, 1);
-    X.zs[2] = z2 + __shfl_xor_sync(0xffffffffu, z2, 1);
+#pragma unroll
+    for (int o = 1; o < 64 / E; o <<= 1) {
+        z0 += __shfl_xor_sync(0xffffffffu, z0, o);
+        z1 += __shfl_xor_sync(0xffffffffu, z1, o);
+        z2 += __shfl_xor_sync(0xffffffffu, z2, o);
+    }
+    X.zs[0] = z0;
+    X.zs[1] = z1;
+    X.zs[2] = z2;
 }
-__device__ __forceinline__ void mma_store_digits(const XDigits& X, int t, int K, uint8_t* act) {
+template <int E>
+__device__ __forceinline__ void mma_store_digits(const XDigits<E>& X, int t, int K, uint8_t* act) {
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
-        uint4* dst = reinterpret_cast<uint4*>(act + d * mma_digit_stride(K) + 32 * t);
-        dst[0] = make_uint4(X.w[d][0], X.w[d][1], X.w[d][2], X.w[d][3]);
-        dst[1] = make_uint4(X.w[d][4], X.w[d][5], X.w[d][6], X.w[d][7]);
+        uint4* dst = reinterpret_cast<uint4*>(act + d * mma_digit_stride(K) + E * t);
+#pragma unroll
+        for (int k = 0; k < E / 16; ++k)
+            dst[k] = make_uint4(X.w[d][4 * k], X.w[d][4 * k + 1], X.w[d][4 * k + 2], X.w[d][4 * k + 3]);
     }
-    if ((t & 1) == 0) {
-        const int g = t >> 1, base = 8 * (g >> 1), n0 = (g & 1) * 3;
+    constexpr int kTpg = 64 / E;  // threads per group
+    if (t % kTpg == 0) {
+        const int g = t / kTpg, base = 8 * (g >> 1), n0 = (g & 1) * 3;
         int* ci = mma_cinit(act, K);
         float* wt = mma_wtab(act, K);
 #pragma unroll
@@ -655,6 +667,53 @@ __device__ __forceinline__ void mma_store_digits(const XDigits& X, int t, int K,
     }
 }
 
+// Prologue of a tensor-core phase over K / E threads, thread t owning columns [E t, E t + E) of
+// the staged x: RMSNorm (rmsnormReference, ref_rmsnorm.cpp:8-17: x * (1 / sqrt(mean(x^2) +
+// eps)) * w) when asked (a gated prologue has already normalised x in place), then the digit
+// table, written over the staged x once every thread has read its columns.
+template <int E>
+__device__ __forceinline__ void mma_prologue(const GemvParams& p, const int pro, Ctx& c, unsigned long long* ts) {
+    const int K = p.cols, nth = K / E;
+    const int tid = c.tid, lane = c.lane, warp = c.warp;
+    XDigits<E> X;
+    if (tid < nth) {
+        const int row = (E * tid) >> 5, ch0 = ((E * tid) & 31) >> 2;
+        float xv[E];
+#pragma unroll
+        for (int i = 0; i < E / 4; ++i) {
+            const float4 a = *staged_chunk(c.act, row, ch0 + i);
+            xv[4 * i] = a.x;
+            xv[4 * i + 1] = a.y;
+            xv[4 * i + 2] = a.z;
+            xv[4 * i + 3] = a.w;
+        }
+        if (pro == kProRms) {
+            float ss = 0.0f;
+#pragma unroll
+            for (int i = 0; i < E; ++i) ss += xv[i] * xv[i];
+            ss = warp_sum(ss);
+            if (lane == 0) c.wsum[warp] = ss;
+            named_bar(2, nth);
+            float tot = 0.0f;
+            for (int w = 0; w < (nth >> 5); ++w) tot += c.wsum[w];
+            const float inv = 1.0f / sqrtf(tot / static_cast<float>(K) + p.eps);
+#pragma unroll
+            for (int i = 0; i < E / 4; ++i) {
+                const float4 g = *staged_chunk(c.act + K, row, ch0 + i);
+                xv[4 * i] = xv[4 * i] * inv * g.x;
+                xv[4 * i + 1] = xv[4 * i + 1] * inv * g.y;
+                xv[4 * i + 2] = xv[4 * i + 2] * inv * g.z;
+                xv[4 * i + 3] = xv[4 * i + 3] * inv * g.w;
+            }
+        }
+        if (ts && tid == 0) ts[3] = global_ns() + (xv[0] != xv[0]);
+        mma_make_digits<E>(xv, X);
+    }
+    named_bar(1, kStepConsumers);  // every staged x read (and wsum): the digit table may overwrite it
+    if (tid < nth) mma_store_digits<E>(X, tid, K, reinterpret_cast<uint8_t*>(c.act));
+    named_bar(1, kStepConsumers);
+}
+
 // One GEMV phase on the tensor cores. Three teams of four warps take this block's 16-row tiles
 // in turn; a team streams a tile's chunks (mma_ppc pairs of groups each) and every warp takes a
 // quarter of each chunk's pairs: per pair four mma.sync (one per 32-column slab) into one
@@ -663,7 +722,7 @@ __device__ __forceinline__ void gemv_phase_mma(const GemvParams& p, const int pr
                                                unsigned long long* ts) {
     int r_begin, r_end, nchunks;
     block_rows(p, &r_begin, &r_end, &nchunks);
-    const int K = p.cols, nth = K >> 5;
+    const int K = p.cols;
     const int tid = c.tid, lane = c.lane, warp = c.warp;
     uint8_t* act = reinterpret_cast<uint8_t*>(c.act);
     float best_v = -INFINITY;
@@ -674,19 +733,11 @@ __device__ __forceinline__ void gemv_phase_mma(const GemvParams& p, const int pr
     mbar_wait_bounded(c.xbar, c.parity, p.err);
     if (ts && tid == 0) ts[10] = global_ns();
     if (pro == kProGatedRms) gated_prologue(p, c);
-    XDigits X;
-    if (tid < nth) {
-        float xv[32];
-        if (pro == kProRms)
-            staged_prologue<kProRms>(p, c.act, tid, lane, warp, 0, nth >> 5, 2, nth, c.wsum, xv);
-        else
-            staged_row(c.act, tid, xv);  // plain, or already normalised by gated_prologue
-        if (ts && tid == 0) ts[3] = global_ns() + (xv[0] != xv[0]);
-        mma_make_digits(xv, X);
-    }
-    named_bar(1, kStepConsumers);  // every staged x read: the digit table may overwrite it
-    if (tid < nth) mma_store_digits(X, tid, K, act);
-    named_bar(1, kStepConsumers);
+    // 16 columns per thread while K / 16 threads fit the consumers (K <= 6144), else 32
+    if (K / 16 <= kStepConsumers)
+        mma_prologue<16>(p, pro, c, ts);
+    else
+        mma_prologue<32>(p, pro, c, ts);
     if (ts && tid == 0) ts[4] = global_ns();
 
     const int tau = warp / kMmaStepWarpsPerTeam, wt = warp % kMmaStepWarpsPerTeam;
