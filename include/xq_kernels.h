@@ -48,6 +48,17 @@ XQK_API int xqk_gemv_w4a16(const xqk_matrix* m, const float* x_dev, float* y_dev
  * of 4096 above 4096), which xqk_matrix_create then also stores in the tensor-core tile
  * layout; other matrices return XQ_ERR_NOT_READY (-2). Finite x only. */
 XQK_API int xqk_gemv_w4a16_mma(const xqk_matrix* m, const float* x_dev, float* y_dev, void* stream);
+/* The tensor-core tile layout of a symmetric matrix, written to a host buffer (host only, no
+ * GPU): no reference counterpart; for packaging pipelines and tests. packed: rows * cols / 2
+ * bytes in the reference's nibble order, scales: rows * cols / 64 fp32 (zero 8 implied, scales
+ * stored as fp16). Per 16-row tile and per 128 columns, 1088 bytes: four 32-column slabs of 256
+ * bytes (lane L's 8 bytes: byte j of word 0 = code(r, c0 + j) | code(r + 8, c0 + j) << 4, word 1
+ * the same for columns c0 + 16 + j, r = 16 * tile + L / 4, c0 = 4 * (L % 4)) then fp16 scales
+ * [row r: group 0, group 1 | row r + 8: group 0, group 1] for r = 0..7. Rows past `rows` are
+ * code 8, scale 0. *written = the size needed; XQ_ERR_BUFFER_TOO_SMALL (-5) if capacity is
+ * short; cols must be a multiple of 128. */
+XQK_API int xqk_mma_tiles(const uint8_t* packed, const float* scales, int rows, int cols, uint8_t* out,
+                          size_t capacity, size_t* written);
 /* Same with host buffers: copies x in, runs, copies y out, synchronises. */
 XQK_API int xqk_gemv_w4a16_host(const xqk_matrix* m, const float* x_host, float* y_host);
 /* argmax_r (W x)[r], ties to the lowest index (gemvW4A16ArgmaxNeon,

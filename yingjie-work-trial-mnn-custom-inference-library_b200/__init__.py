@@ -36,6 +36,7 @@ KERNEL_SYMBOLS = [
     "xqk_last_error", "xqk_matrix_create", "xqk_matrix_destroy", "xqk_matrix_info", "xqk_gemv_w4a16",
     "xqk_gemv_w4a16_host", "xqk_gemv_w4a16_argmax", "xqk_rmsnorm", "xqk_gated_delta_step",
     "xqk_attention_step", "xqk_attention_step_noalloc", "xqk_gemv_w4a16_mma",
+    "xqk_mma_tiles",
 ]
 
 
@@ -104,6 +105,7 @@ def lib():
                                   C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]
     L.xqk_gemv_w4a16.argtypes = [P, P, P, P]
     L.xqk_gemv_w4a16_mma.argtypes = [P, P, P, P]
+    L.xqk_mma_tiles.argtypes = [P, P, C.c_int, C.c_int, P, C.c_size_t, C.POINTER(C.c_size_t)]
     L.xqk_gemv_w4a16_host.argtypes = [P, P, P]
     L.xqk_gemv_w4a16_argmax.argtypes = [P, P, P, P, P]
     L.xqk_rmsnorm.argtypes = [P, P, C.c_int, C.c_float, P, P]

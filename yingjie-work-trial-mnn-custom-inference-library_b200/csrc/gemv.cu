@@ -628,6 +628,21 @@ int xqk_gemv_w4a16_mma(const xqk_matrix* m, const float* x_dev, float* y_dev, vo
                                                                                                               : -4;
 }
 
+int xqk_mma_tiles(const uint8_t* packed, const float* scales, int rows, int cols, uint8_t* out, size_t capacity,
+                  size_t* written) {
+    if (!packed || !scales || !written || rows <= 0 || cols <= 0 || cols % 128 != 0) {
+        xqb::set_last_error("xqk_mma_tiles: invalid argument (cols must be a multiple of 128)");
+        return -1;
+    }
+    const size_t need = static_cast<size_t>((rows + 15) / 16) * (cols / 128) * xqb::kMmaUnitBytes;
+    *written = need;
+    if (!out || capacity < need) return -5;
+    std::vector<uint8_t> t;
+    if (!xqb::host_mma_tiles(packed, scales, rows, cols, &t)) return -1;
+    std::memcpy(out, t.data(), need);
+    return 0;
+}
+
 int xqk_gemv_w4a16_host(const xqk_matrix* m, const float* x_host, float* y_host) {
     if (!m || !x_host || !y_host) return -1;
     if (cudaSetDevice(m->device) != cudaSuccess) return -4;

@@ -331,6 +331,19 @@ bool attach_mma_tiles(const std::vector<uint8_t>& rows_host, DevMatrix* m, std::
     return true;
 }
 
+bool host_mma_tiles(const uint8_t* packed, const float* scales, int rows, int cols, std::vector<uint8_t>* out) {
+    if (!packed || !scales || rows <= 0 || cols <= 0 || cols % 128 != 0) return false;
+    const int K = cols, gpr = K / 64;
+    fill_tiles(
+        rows, K,
+        [&](int r, int c) -> uint32_t {
+            const uint8_t b = packed[static_cast<size_t>(r) * (K / 2) + c / 2];
+            return (c & 1) ? (b >> 4) : (b & 15u);
+        },
+        [&](int r, int g) { return __float2half_rn(scales[static_cast<size_t>(r) * gpr + g]); }, out);
+    return true;
+}
+
 void free_mma_matrix(MmaMatrix* m) {
     cudaFree(m->d_tiles);
     *m = MmaMatrix();

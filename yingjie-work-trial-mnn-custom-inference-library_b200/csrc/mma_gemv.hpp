@@ -29,6 +29,9 @@ void free_mma_matrix(MmaMatrix* m);
 // Build the tile copy of a symmetric row-layout matrix from its host rows (as
 // build_matrix_rows / read_b200_file give them) into m->d_tiles.
 bool attach_mma_tiles(const std::vector<uint8_t>& rows_host, DevMatrix* m, std::string* error);
+// The tiles of a symmetric matrix (reference nibble order, fp32 scales rounded to fp16) in host
+// memory; cols a multiple of 128. No device work.
+bool host_mma_tiles(const uint8_t* packed, const float* scales, int rows, int cols, std::vector<uint8_t>* out);
 bool mma_init_device();
 // y = W x (fp32 in/out, device pointers); one block per SM, at most num_sms blocks.
 bool launch_mma_gemv(const MmaMatrix& m, const float* x, float* y, unsigned* err, int num_sms, cudaStream_t s);
