@@ -17,13 +17,14 @@ namespace {
 // Shared-memory layout (bytes):
 //   [0, 128)      full mbarriers       [128, 256)    empty mbarriers
 //   [256, 384)    warp sums            [384, 416)    activation / constant / 2 descriptor mbarriers
-//   [512, 4608)   double-buffered row sums [2][16][32]
+//   [512, 4608)   row sums: dp4a path [2][16][32]; tensor-core path [3 teams][2][4 warps][16]
 //   [4608, 6912)  attention scratch    [6912, 8192)  3 DeltaNet scratches
 //   [8192, 8704)  argmax scratch       [8704, 9728)  two phase descriptors
 //   [10240, +48K) activation area: a GEMV phase's x and its second vector (norm weights or
-//                 gate) as 128-byte rows with 128-byte swizzle, or an attention phase's q / scores
+//                 gate) as 128-byte rows with 128-byte swizzle (the tensor-core path then writes
+//                 x's digit table over them), or an attention phase's q / scores
 //   [.., +4K)     epilogue inputs of this block's rows (residual, conv weights and state)
-//   then the weight ring.
+//   then the weight ring (slot size StepParams::slot_bytes).
 constexpr int kOffFull = 0, kOffEmpty = 128, kOffWsum = 256, kOffXBar = 384, kOffCBar = 392, kOffDBar = 400,
               kOffRed = 512, kOffAttn = 4608, kOffDelta = 6912, kOffArg = 8192, kOffDesc = kStepHeaderBytes;
 constexpr int kDescBytes = 512;

@@ -4,9 +4,9 @@
 // list and streams this block's share of every weight matrix, in order, through one
 // shared-memory ring (1-D bulk copies, full/empty mbarriers). It never waits for
 // activations, so HBM streaming continues across phase boundaries and across the grid
-// barriers the consumers wait on. The other warps run the phases: fused W4A16 GEMVs (the
-// same device math as gemv_w4a16_kernel), Gated-DeltaNet and attention work items, the
-// embedding load of a prefill step. Consecutive phases are separated by a grid barrier
+// barriers the consumers wait on. The other warps run the phases: fused W4A16 GEMVs (on the
+// integer tensor cores over 16-row tiles, kMetaMma, or the dp4a row loop of gemv_w4a16_kernel),
+// Gated-DeltaNet and attention work items, the embedding load of a prefill step. Consecutive phases are separated by a grid barrier
 // (global arrival counter, bounded spin).
 #pragma once
 
@@ -32,7 +32,7 @@ struct alignas(16) PhaseDesc {  // copied into shared memory with one bulk copy
 constexpr int kStepConsumers = 384;                    // 12 warps
 constexpr int kStepThreads = kStepConsumers + 32;      // + producer warp
 constexpr int kStepMaxSlots = 16;
-constexpr int kStepSlotBytes = 26112;                  // 12 rows of K=4096 or 4 rows of K=12288
+constexpr int kStepSlotBytes = 26112;                  // dp4a rows: 12 of K=4096 or 4 of K=12288
 constexpr int kMmaStepSlotBytes = 34816;               // tensor-core tiles: 32 pairs of groups x 16 rows (default)
 constexpr int kStepAttnDynBytes = 24 * 1024;           // q [group][hd] + scores [group][cmax]
 constexpr int kStepHeaderBytes = 8704;
