@@ -9,6 +9,9 @@
 #include <sys/stat.h>
 #include <array>
 #include <map>
+#include <climits>
+#include <memory>
+#include <mutex>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -132,19 +135,14 @@ ModelDims parse_manifest(const std::string& js, int* n_layers) {
 }
 
 DeviceModel::~DeviceModel() {
-    if (!stream_ && allocs_.empty()) return;
+    if (!stream_ && allocs_.empty()) return;  // (weights_ releases itself)
     cudaSetDevice(opts_.device);
     if (stream_) cudaStreamSynchronize(stream_);
     destroy_graphs();
-    for (DevLayer& L : layers_) {
-        free_matrix(&L.in_proj);
-        free_matrix(&L.out_proj);
-        free_matrix(&L.gate_up);
-        free_matrix(&L.down);
+    for (DevLayer& L : layers_) {  // matrices and weights belong to weights_
         cudaFree(L.k_cache);
         cudaFree(L.v_cache);
     }
-    free_matrix(&lm_head_);
     cudaFree(d_rope_);
     cudaFree(d_phases_decode_);
     cudaFree(d_tmaps_);
@@ -291,6 +289,175 @@ bool pack_b200_layout(const std::string& dir, std::string* error) {
     return true;
 }
 
+// Read-only device weights of one package on one device, shared by every session that loads
+// the same package there (the reference's sessions each hold a CustomModel; on the GPU the
+// 4.2 GB of matrices, their tile copy and the 2 GB embedding table are loaded once per
+// device): fused matrices (+ tensor-core tiles), norm and conv weights, gates, final norm,
+// embeddings. Freed when the last session releases it.
+struct SharedWeights {
+    int device = 0;
+    std::vector<DevLayer> layers;  // weight fields only; states stay null
+    DevMatrix lm_head;
+    float* final_norm = nullptr;
+    uint16_t* emb = nullptr;
+    bool packed_layout = false;
+    size_t weight_bytes = 0, device_bytes = 0;
+    std::vector<void*> allocs;
+
+    bool alloc(void** p, size_t bytes, std::string* error) {
+        *p = nullptr;
+        if (cudaMalloc(p, std::max<size_t>(1, bytes)) != cudaSuccess) {
+            *error = "device allocation failed for the shared weights";
+            return false;
+        }
+        allocs.push_back(*p);
+        device_bytes += bytes;
+        return true;
+    }
+    bool upload(float** dst, const std::vector<float>& v, std::string* error) {
+        if (!alloc(reinterpret_cast<void**>(dst), v.size() * 4, error)) return false;
+        if (cudaMemcpy(*dst, v.data(), v.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
+            *error = "vector upload failed";
+            return false;
+        }
+        return true;
+    }
+    ~SharedWeights() {
+        int prev = 0;
+        cudaGetDevice(&prev);
+        cudaSetDevice(device);
+        for (DevLayer& L : layers) {
+            free_matrix(&L.in_proj);
+            free_matrix(&L.out_proj);
+            free_matrix(&L.gate_up);
+            free_matrix(&L.down);
+        }
+        free_matrix(&lm_head);
+        for (void* q : allocs) cudaFree(q);
+        cudaSetDevice(prev);
+    }
+};
+
+namespace {
+std::mutex g_weights_mu;
+std::map<std::string, std::weak_ptr<SharedWeights>> g_weights;  // canonical dir | device | tiles
+
+bool load_shared_weights(const std::string& dir, const ModelDims& d, int n_layers, bool want_tiles, SharedWeights* w,
+                         std::string* error) {
+    std::vector<float> v;
+    if (!read_vec(dir + "/norm_weight.f32", d.hidden, &v, error)) return false;
+    add_one(&v);
+    if (!w->upload(&w->final_norm, v, error)) return false;
+    // Weight matrices: the packed B200 layout (b200/*.b200, written by the packer) when present,
+    // else the xq4 files re-tiled here. Either way every matrix is checked against the
+    // manifest's shapes.
+    w->layers.resize(static_cast<size_t>(n_layers));
+    {
+        std::vector<bool> full;
+        const std::vector<FusedSpec> specs = fused_specs(dir, d, n_layers, &full);
+        w->packed_layout = file_exists(dir + kB200LayoutFile);
+        for (const FusedSpec& sp : specs) {
+            DevMatrix shape;
+            std::vector<uint8_t> host;
+            if (w->packed_layout) {
+                if (!read_b200_file(dir + "/b200/" + sp.name + ".b200", &shape, &host, error)) return false;
+                int rows = 0;
+                for (const auto& sh : sp.shapes) rows += sh.first;
+                if (shape.rows != rows || shape.cols != sp.shapes[0].second || shape.group != 64) {
+                    *error = "packed B200 matrix " + sp.name + " does not match the manifest; re-run the packer";
+                    return false;
+                }
+            } else if (!build_spec_rows(sp, &shape, &host, error)) {
+                return false;
+            }
+            DevMatrix* dst = &w->lm_head;
+            if (sp.layer >= 0) {
+                DevLayer& L = w->layers[static_cast<size_t>(sp.layer)];
+                L.full = full[static_cast<size_t>(sp.layer)];
+                dst = sp.slot == 0 ? &L.in_proj : sp.slot == 1 ? &L.out_proj : sp.slot == 2 ? &L.gate_up : &L.down;
+            }
+            *dst = shape;
+            if (!upload_matrix_rows(host, dst, error)) return false;
+            w->weight_bytes += dst->bytes;
+            w->device_bytes += dst->bytes;
+            if (want_tiles && dst->kind == 0) {
+                if (!attach_mma_tiles(host, dst, error)) return false;
+                w->device_bytes += dst->tile_bytes;
+            }
+        }
+    }
+    for (int i = 0; i < n_layers; ++i) {
+        DevLayer& L = w->layers[static_cast<size_t>(i)];
+        const std::string p = dir + "/layers_" + std::to_string(i) + "_";
+        if (!read_vec(p + "input_layernorm_weight.f32", d.hidden, &v, error)) return false;
+        add_one(&v);
+        if (!w->upload(&L.input_norm, v, error)) return false;
+        if (!read_vec(p + "post_attention_layernorm_weight.f32", d.hidden, &v, error)) return false;
+        add_one(&v);
+        if (!w->upload(&L.post_norm, v, error)) return false;
+        if (L.full) {  // set with the layer's matrices above
+            if (!read_vec(p + "self_attn_q_norm_weight.f32", d.head_dim, &v, error)) return false;
+            add_one(&v);
+            if (!w->upload(&L.q_norm, v, error)) return false;
+            if (!read_vec(p + "self_attn_k_norm_weight.f32", d.head_dim, &v, error)) return false;
+            add_one(&v);
+            if (!w->upload(&L.k_norm, v, error)) return false;
+        } else {
+            if (!read_vec(p + "linear_attn_norm_weight.f32", d.lv_hd, &v, error)) return false;
+            if (!w->upload(&L.lin_norm, v, error)) return false;
+            if (!read_vec(p + "linear_attn_conv1d_weight.f32", d.conv_dim * d.conv_k, &v, error)) return false;
+            if (!w->upload(&L.conv_w, v, error)) return false;
+            if (!read_vec(p + "linear_attn_A_log.f32", d.lv_heads, &v, error)) return false;
+            if (!w->upload(&L.a_log, v, error)) return false;
+            if (!read_vec(p + "linear_attn_dt_bias.f32", d.lv_heads, &v, error)) return false;
+            if (!w->upload(&L.dt_bias, v, error)) return false;
+        }
+        for (const DevMatrix* m : {&L.in_proj, &L.out_proj, &L.gate_up, &L.down}) {
+            if (!m->fast()) {
+                *error = "layer " + std::to_string(i) + ": matrix shape not supported by the fused kernels";
+                return false;
+            }
+        }
+    }
+    if (!w->lm_head.fast()) {
+        *error = "lm_head shape not supported by the fused kernels";
+        return false;
+    }
+    // Embedding table, resident in device memory (the reference reads one row from disk
+    // per token, custom_model.cpp:569-608).
+    {
+        const size_t bytes = static_cast<size_t>(d.vocab) * d.hidden * 2;
+        std::ifstream in(dir + "/embeddings_bf16.bin", std::ios::binary);
+        if (!w->alloc(reinterpret_cast<void**>(&w->emb), bytes, error)) return false;
+        const size_t chunk = 64u << 20;
+        void* staging = nullptr;
+        if (cudaMallocHost(&staging, chunk) != cudaSuccess) {
+            *error = "pinned staging allocation failed";
+            return false;
+        }
+        size_t done = 0;
+        bool ok = true;
+        while (done < bytes && ok) {
+            const size_t n = std::min(chunk, bytes - done);
+            in.read(static_cast<char*>(staging), static_cast<std::streamsize>(n));
+            if (in.gcount() != static_cast<std::streamsize>(n)) {
+                ok = false;
+                break;
+            }
+            ok = cudaMemcpy(reinterpret_cast<uint8_t*>(w->emb) + done, staging, n, cudaMemcpyHostToDevice) ==
+                 cudaSuccess;
+            done += n;
+        }
+        cudaFreeHost(staging);
+        if (!ok) {
+            *error = "short embeddings_bf16.bin";
+            return false;
+        }
+    }
+    return true;
+}
+}  // namespace
+
 bool DeviceModel::load(const std::string& dir, const Options& opts, std::string* error) {
     opts_ = opts;
     if (cudaSetDevice(opts.device) != cudaSuccess) {
@@ -328,123 +495,40 @@ bool DeviceModel::load(const std::string& dir, const Options& opts, std::string*
         *error = "missing embeddings_bf16.bin";
         return false;
     }
-    std::vector<float> v;
-    if (!read_vec(dir + "/norm_weight.f32", d.hidden, &v, error)) return false;
-    add_one(&v);
-    if (!upload_vec(&d_final_norm_, v, error)) return false;
-    // Weight matrices: the packed B200 layout (b200/*.b200, written by the packer) when present,
-    // else the xq4 files re-tiled here. Either way every matrix is checked against the
-    // manifest's shapes.
-    layers_.resize(static_cast<size_t>(n_layers));
     // Tensor-core tiles for the step kernel (XQ_STEP_MMA=0 keeps the dp4a row loop): a second
     // copy of every symmetric matrix in 16-row tiles, built from the same host rows.
     const char* em = std::getenv("XQ_STEP_MMA");
     const char* ep = std::getenv("XQ_PERSISTENT");
     const bool want_tiles = opts.persistent && !(ep && std::atoi(ep) == 0) && !(em && std::atoi(em) == 0);
     {
-        std::vector<bool> full;
-        const std::vector<FusedSpec> specs = fused_specs(dir, d, n_layers, &full);
-        packed_layout_ = file_exists(dir + kB200LayoutFile);
-        for (const FusedSpec& sp : specs) {
-            DevMatrix shape;
-            std::vector<uint8_t> host;
-            if (packed_layout_) {
-                if (!read_b200_file(dir + "/b200/" + sp.name + ".b200", &shape, &host, error)) return false;
-                int rows = 0;
-                for (const auto& sh : sp.shapes) rows += sh.first;
-                if (shape.rows != rows || shape.cols != sp.shapes[0].second || shape.group != 64) {
-                    *error = "packed B200 matrix " + sp.name + " does not match the manifest; re-run the packer";
-                    return false;
-                }
-            } else if (!build_spec_rows(sp, &shape, &host, error)) {
-                return false;
-            }
-            DevMatrix* dst = &lm_head_;
-            if (sp.layer >= 0) {
-                DevLayer& L = layers_[static_cast<size_t>(sp.layer)];
-                L.full = full[static_cast<size_t>(sp.layer)];
-                dst = sp.slot == 0 ? &L.in_proj : sp.slot == 1 ? &L.out_proj : sp.slot == 2 ? &L.gate_up : &L.down;
-            }
-            *dst = shape;
-            if (!upload_matrix_rows(host, dst, error)) return false;
-            weight_bytes_ += dst->bytes;
-            device_bytes_ += dst->bytes;
-            if (want_tiles && dst->kind == 0) {
-                if (!attach_mma_tiles(host, dst, error)) return false;
-                device_bytes_ += dst->tile_bytes;
-            }
+        // Weights: shared with the other live sessions of this package on this device.
+        char real[PATH_MAX];
+        const std::string canon = realpath(dir.c_str(), real) ? std::string(real) : dir;
+        const std::string key = canon + "|" + std::to_string(opts.device) + "|" + (want_tiles ? "tiles" : "rows");
+        std::lock_guard<std::mutex> lock(g_weights_mu);
+        auto it = g_weights.find(key);
+        if (it != g_weights.end()) weights_ = it->second.lock();
+        weights_reused_ = weights_ != nullptr;
+        if (!weights_) {
+            auto w = std::make_shared<SharedWeights>();
+            w->device = opts.device;
+            if (!load_shared_weights(dir, d, n_layers, want_tiles, w.get(), error)) return false;
+            g_weights[key] = w;
+            weights_ = w;
         }
     }
-    for (int i = 0; i < n_layers; ++i) {
-        DevLayer& L = layers_[static_cast<size_t>(i)];
-        const std::string p = dir + "/layers_" + std::to_string(i) + "_";
-        if (!read_vec(p + "input_layernorm_weight.f32", d.hidden, &v, error)) return false;
-        add_one(&v);
-        if (!upload_vec(&L.input_norm, v, error)) return false;
-        if (!read_vec(p + "post_attention_layernorm_weight.f32", d.hidden, &v, error)) return false;
-        add_one(&v);
-        if (!upload_vec(&L.post_norm, v, error)) return false;
-        if (L.full) {  // set with the layer's matrices above
-            if (!read_vec(p + "self_attn_q_norm_weight.f32", d.head_dim, &v, error)) return false;
-            add_one(&v);
-            if (!upload_vec(&L.q_norm, v, error)) return false;
-            if (!read_vec(p + "self_attn_k_norm_weight.f32", d.head_dim, &v, error)) return false;
-            add_one(&v);
-            if (!upload_vec(&L.k_norm, v, error)) return false;
-        } else {
-            if (!read_vec(p + "linear_attn_norm_weight.f32", d.lv_hd, &v, error)) return false;
-            if (!upload_vec(&L.lin_norm, v, error)) return false;
-            if (!read_vec(p + "linear_attn_conv1d_weight.f32", d.conv_dim * d.conv_k, &v, error)) return false;
-            if (!upload_vec(&L.conv_w, v, error)) return false;
-            if (!read_vec(p + "linear_attn_A_log.f32", d.lv_heads, &v, error)) return false;
-            if (!upload_vec(&L.a_log, v, error)) return false;
-            if (!read_vec(p + "linear_attn_dt_bias.f32", d.lv_heads, &v, error)) return false;
-            if (!upload_vec(&L.dt_bias, v, error)) return false;
-            if (!dev_alloc(&L.conv_state, static_cast<size_t>(d.conv_dim) * std::max(0, d.conv_k - 1), error) ||
-                !dev_alloc(&L.rec_state, static_cast<size_t>(d.lv_heads) * d.lk_hd * d.lv_hd, error))
-                return false;
-        }
-        for (const DevMatrix* m : {&L.in_proj, &L.out_proj, &L.gate_up, &L.down}) {
-            if (!m->fast()) {
-                *error = "layer " + std::to_string(i) + ": matrix shape not supported by the fused kernels";
-                return false;
-            }
-        }
-    }
-    if (!lm_head_.fast()) {
-        *error = "lm_head shape not supported by the fused kernels";
-        return false;
-    }
-    // Embedding table, resident in device memory (the reference reads one row from disk
-    // per token, custom_model.cpp:569-608).
-    {
-        const size_t bytes = static_cast<size_t>(d.vocab) * d.hidden * 2;
-        std::ifstream in(dir + "/embeddings_bf16.bin", std::ios::binary);
-        if (!dev_alloc(&d_emb_, bytes / 2, error)) return false;
-        const size_t chunk = 64u << 20;
-        void* staging = nullptr;
-        if (cudaMallocHost(&staging, chunk) != cudaSuccess) {
-            *error = "pinned staging allocation failed";
+    layers_ = weights_->layers;
+    lm_head_ = weights_->lm_head;
+    d_final_norm_ = weights_->final_norm;
+    d_emb_ = weights_->emb;
+    packed_layout_ = weights_->packed_layout;
+    weight_bytes_ = weights_->weight_bytes;
+    device_bytes_ += weights_->device_bytes;
+    for (DevLayer& L : layers_) {  // this session's DeltaNet states
+        if (L.full) continue;
+        if (!dev_alloc(&L.conv_state, static_cast<size_t>(d.conv_dim) * std::max(0, d.conv_k - 1), error) ||
+            !dev_alloc(&L.rec_state, static_cast<size_t>(d.lv_heads) * d.lk_hd * d.lv_hd, error))
             return false;
-        }
-        size_t done = 0;
-        bool ok = true;
-        while (done < bytes && ok) {
-            const size_t n = std::min(chunk, bytes - done);
-            in.read(static_cast<char*>(staging), static_cast<std::streamsize>(n));
-            if (in.gcount() != static_cast<std::streamsize>(n)) {
-                ok = false;
-                break;
-            }
-            ok = cudaMemcpy(reinterpret_cast<uint8_t*>(d_emb_) + done, staging, n, cudaMemcpyHostToDevice) ==
-                 cudaSuccess;
-            done += n;
-        }
-        cudaFreeHost(staging);
-        if (!ok) {
-            *error = "short embeddings_bf16.bin";
-            return false;
-        }
     }
     const int qkv_rows = 2 * d.heads * d.head_dim + 2 * d.kv_heads * d.head_dim;
     const int group = d.heads / d.kv_heads;

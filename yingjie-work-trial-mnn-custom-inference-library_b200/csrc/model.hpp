@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <memory>
 #include <string>
 #include <vector>
 
@@ -49,6 +50,8 @@ struct DevLayer {
 // dir/b200/*.b200 plus dir/b200/layout.json (host only, no GPU needed); the loader then reads
 // them instead of re-tiling the xq4 files.
 bool pack_b200_layout(const std::string& dir, std::string* error);
+
+struct SharedWeights;
 
 struct Options {
     int device = 0;
@@ -102,6 +105,10 @@ public:
     bool persistent() const { return persistent_; }
     bool tensor_core_step() const { return persistent_ && meta_kind_ == kMetaMma; }
     bool packed_layout() const { return packed_layout_; }
+    // Whether this session found its weights already loaded by another live session.
+    bool weights_reused() const { return weights_reused_; }
+    // Sessions (this one included) currently holding this session's weights.
+    long weights_users() const { return weights_.use_count(); }
     cudaStream_t stream() const { return stream_; }
     const std::vector<DevLayer>& layers() const { return layers_; }
     const DevMatrix& lm_head() const { return lm_head_; }
@@ -169,6 +176,8 @@ private:
     PhaseDesc* d_phases_decode_ = nullptr;
     void* d_tmaps_ = nullptr;  // CUtensorMap array of the phase lists
     bool packed_layout_ = false;  // weights read from b200/*.b200
+    std::shared_ptr<SharedWeights> weights_;  // read-only weights, shared per package and device
+    bool weights_reused_ = false;
     unsigned long long* d_block_done_ = nullptr;  // XQ_STEP_TRACE >= 2: per-block phase finish times
     std::vector<double> block_late_ns_;
     std::vector<double> barrier_ns_;

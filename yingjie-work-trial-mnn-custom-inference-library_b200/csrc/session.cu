@@ -397,7 +397,9 @@ public:
             << ",\"kernels_per_decode_step\":" << model_->kernels_per_decode_step()
             << ",\"persistent_step_kernel\":" << (model_->persistent() ? "true" : "false")
             << ",\"packed_layout\":" << (model_->packed_layout() ? "true" : "false")
-            << ",\"tensor_core_gemv\":" << (model_->tensor_core_step() ? "true" : "false");
+            << ",\"tensor_core_gemv\":" << (model_->tensor_core_step() ? "true" : "false")
+            << ",\"weights_reused\":" << (model_->weights_reused() ? "true" : "false")
+            << ",\"weights_users\":" << model_->weights_users();
         if (model_ && !model_->phase_trace_summary().empty())
             o << ",\"step_phase_trace\":" << model_->phase_trace_summary();
         o << ",\"selected_kernels\":\"" << json_escape(coverage()) << "\"}";
