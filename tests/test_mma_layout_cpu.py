@@ -144,8 +144,9 @@ def seeded(rows, cols, seed):
     return packed, s, x
 
 
-@pytest.mark.parametrize("rows,cols", [(37, 256), (16, 128), (5, 512)])
+@pytest.mark.parametrize("rows,cols", [(37, 256), (16, 128), (5, 512), (8200, 128)])
 def test_tiles_match_documented_layout(rows, cols):
+    """(8200 rows: more than 512 tiles, built by several host threads.)"""
     packed, s, _ = seeded(rows, cols, rows)
     assert np.array_equal(tiles_from_lib(packed, s, rows, cols), expected_tiles(packed, s, rows, cols))
 

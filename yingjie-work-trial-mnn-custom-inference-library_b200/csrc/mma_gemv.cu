@@ -18,6 +18,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <thread>
 #include <vector>
 
 #include "common.cuh"
@@ -235,36 +236,57 @@ namespace {
 
 // The mma16 tiles of a rows x K matrix given code(row, col) and scale(row, group); rows past
 // `rows` are padding (code 8, scale 0: they contribute exact zeros).
+// One 16-row tile: per pair of groups, four slabs of fragment-ordered nibbles, then the scales.
+template <class Cd, class Sc>
+void fill_one_tile(int tile, int pairs, std::vector<uint8_t>* out, const Cd& cd, const Sc& sc) {
+    for (int pp = 0; pp < pairs; ++pp) {
+        uint8_t* blk = out->data() + (static_cast<size_t>(tile) * pairs + pp) * kMmaUnitBytes;
+        for (int sl = 0; sl < 4; ++sl) {
+            const int col = 128 * pp + 32 * sl;
+            for (int L = 0; L < 32; ++L) {
+                const int r = 16 * tile + (L >> 2), c0 = col + (L & 3) * 4;
+                for (int j = 0; j < 4; ++j) {
+                    blk[sl * 256 + 8 * L + j] = static_cast<uint8_t>(cd(r, c0 + j) | (cd(r + 8, c0 + j) << 4));
+                    blk[sl * 256 + 8 * L + 4 + j] =
+                        static_cast<uint8_t>(cd(r, c0 + 16 + j) | (cd(r + 8, c0 + 16 + j) << 4));
+                }
+            }
+        }
+        __half* s = reinterpret_cast<__half*>(blk + 1024);
+        for (int rr = 0; rr < 8; ++rr) {
+            const int r = 16 * tile + rr;
+            s[4 * rr] = sc(r, 2 * pp);
+            s[4 * rr + 1] = sc(r, 2 * pp + 1);
+            s[4 * rr + 2] = sc(r + 8, 2 * pp);
+            s[4 * rr + 3] = sc(r + 8, 2 * pp + 1);
+        }
+    }
+}
+
+// Tiles are independent: host threads take contiguous ranges of them (a 9B package is ~8e9
+// codes, tens of seconds on one core).
 template <class Code, class Scale>
 void fill_tiles(int rows, int K, Code code, Scale scale, std::vector<uint8_t>* out) {
     const int pairs = K / 128, ntiles = (rows + 15) / 16;
     out->assign(static_cast<size_t>(ntiles) * pairs * kMmaUnitBytes, 0);
     auto cd = [&](int r, int c) -> uint32_t { return r < rows ? code(r, c) : 8u; };
     auto sc = [&](int r, int g) -> __half { return r < rows ? scale(r, g) : __float2half_rn(0.0f); };
-    for (int tile = 0; tile < ntiles; ++tile)
-        for (int pp = 0; pp < pairs; ++pp) {
-            uint8_t* blk = out->data() + (static_cast<size_t>(tile) * pairs + pp) * kMmaUnitBytes;
-            for (int sl = 0; sl < 4; ++sl) {
-                const int col = 128 * pp + 32 * sl;
-                for (int L = 0; L < 32; ++L) {
-                    const int r = 16 * tile + (L >> 2), c0 = col + (L & 3) * 4;
-                    for (int j = 0; j < 4; ++j) {
-                        blk[sl * 256 + 8 * L + j] = static_cast<uint8_t>(cd(r, c0 + j) | (cd(r + 8, c0 + j) << 4));
-                        blk[sl * 256 + 8 * L + 4 + j] =
-                            static_cast<uint8_t>(cd(r, c0 + 16 + j) | (cd(r + 8, c0 + 16 + j) << 4));
-                    }
-                }
-            }
-            __half* s = reinterpret_cast<__half*>(blk + 1024);
-            for (int rr = 0; rr < 8; ++rr) {
-                const int r = 16 * tile + rr;
-                s[4 * rr] = sc(r, 2 * pp);
-                s[4 * rr + 1] = sc(r, 2 * pp + 1);
-                s[4 * rr + 2] = sc(r + 8, 2 * pp);
-                s[4 * rr + 3] = sc(r + 8, 2 * pp + 1);
-            }
-        }
+    auto fill_range = [&](int t0, int t1) {
+        for (int tile = t0; tile < t1; ++tile) fill_one_tile(tile, pairs, out, cd, sc);
+    };
+    const int hw = static_cast<int>(std::max(1u, std::thread::hardware_concurrency()));
+    const int nthreads = std::max(1, std::min({hw, 64, ntiles / 256}));
+    if (nthreads == 1) {
+        fill_range(0, ntiles);
+        return;
+    }
+    std::vector<std::thread> pool;
+    for (int k = 0; k < nthreads; ++k)
+        pool.emplace_back(fill_range, static_cast<int>(static_cast<long long>(ntiles) * k / nthreads),
+                          static_cast<int>(static_cast<long long>(ntiles) * (k + 1) / nthreads));
+    for (std::thread& t : pool) t.join();
 }
+
 
 bool upload_tiles(const std::vector<uint8_t>& t, uint8_t** dst, std::string* error) {
     if (cudaMalloc(dst, t.size()) != cudaSuccess ||
