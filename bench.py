@@ -212,6 +212,7 @@ def job_rate(units_per_rank: int, world: int, seconds_max: float) -> float:
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return 0
+    __graft_entry__.load_package()  # registers the package module for the synthetic data generator
     d = make_package(0, 1)
     steps = max(1, min(args.steps, 16))
     warm = min(args.warmup, 1)
