@@ -30,6 +30,24 @@ def test_small_model_matches_reference_golden(small_session):
     assert rel_err(s.hidden(), G["hidden_after"]) <= 1e-4
 
 
+@pytest.mark.parametrize("mma", ["1", "0"])
+def test_step_gemv_engines_match_reference_golden(small_pkg, monkeypatch, mma):
+    """Both GEMV engines of the step kernel (integer tensor cores, and the dp4a row loop that
+    XQ_STEP_MMA=0 selects) against the reference's golden outputs."""
+    monkeypatch.setenv("XQ_STEP_MMA", mma)
+    s = PKG.Session(small_pkg, device=0)
+    try:
+        info = json.loads(s.json("backend"))
+        assert info["persistent_step_kernel"] and info["tensor_core_gemv"] == (mma == "1")
+        s.prefill(G["ids"])
+        assert rel_err(s.hidden(), G["hidden_prefill"]) <= 1e-4
+        toks = [s.decode_one() for _ in range(len(G["tokens"]))]
+        assert toks == list(G["tokens"])
+        assert rel_err(s.hidden(), G["hidden_after"]) <= 1e-4
+    finally:
+        s.close()
+
+
 def test_generate_equals_decode_loop(small_session):
     s = small_session
     out, m = s.generate(G["ids"], len(G["tokens"]))
