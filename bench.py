@@ -130,13 +130,16 @@ def step_roofline(alg_bytes, ms_per_step, peak_gbs):
             "launch_us": round(ms_per_step * 1000, 2)}
 
 
-def gemv_roofline(pkg, peak_gbs, iters=40):
-    """The standalone fused W4A16 GEMV kernel (the per-op path and the kernel-level C ABI) at
-    the largest per-layer shape of the 9B step (gate+up: 24576 x 4096), timed with CUDA events
-    on the launching stream, rotating over 4 copies (214 MB, more than L2)."""
+def gemv_roofline(pkg, peak_gbs, iters=40, engine="dp4a", rows=24576, cols=4096):
+    """A standalone W4A16 GEMV kernel of the kernel-level C ABI, timed with CUDA events on the
+    launching stream: engine "dp4a" (gemv_w4a16_kernel, also the per-op path) or "mma" (the
+    tensor-core gemv_mma_kernel, xqk_gemv_w4a16_mma). The default shape is the largest
+    per-layer matrix of the 9B step (gate+up: 24576 x 4096), rotating over copies that together
+    exceed L2; the lm_head shape (248320 x 4096, 540 MB) needs one copy."""
     import torch
 
-    rows, cols, ncopy = 24576, 4096, 4
+    one = rows * cols // 2 + rows * (cols // 64) * 2
+    ncopy = max(1, min(4, -(-200_000_000 // one)))
     mats = []
     for i in range(ncopy):
         rng = np.random.default_rng(100 + i)
@@ -146,22 +149,27 @@ def gemv_roofline(pkg, peak_gbs, iters=40):
     x = torch.randn(cols, device="cuda")
     y = torch.zeros(rows, device="cuda")
     st = torch.cuda.current_stream()
+
+    def run(m):
+        (m.gemv_mma if engine == "mma" else m.gemv)(x.data_ptr(), y.data_ptr(), st.cuda_stream)
+
     for m in mats:
-        m.gemv(x.data_ptr(), y.data_ptr(), st.cuda_stream)
+        run(m)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(st)
     for i in range(iters):
-        mats[i % ncopy].gemv(x.data_ptr(), y.data_ptr(), st.cuda_stream)
+        run(mats[i % ncopy])
     e1.record(st)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / iters
-    alg = rows * cols // 2 + rows * (cols // 64) * 2 + 4 * cols + 4 * rows
+    alg = one + 4 * cols + 4 * rows
     achieved = alg / (ms * 1e-3) / 1e9
     for m in mats:
         m.close()
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
-            "frac": round(achieved / peak_gbs, 4), "kernel": "gemv_w4a16_kernel",
+            "frac": round(achieved / peak_gbs, 4),
+            "kernel": "gemv_mma_kernel" if engine == "mma" else "gemv_w4a16_kernel",
             "shape": f"{rows}x{cols}", "algorithmic_bytes": alg, "launch_us": round(ms * 1000, 2)}
 
 
@@ -297,7 +305,10 @@ def main():
         print(json.dumps({"step_phase_trace": info["step_phase_trace"]}), file=sys.stderr, flush=True)
     kernels_per_step = int(info.get("kernels_per_decode_step", 0))
     peak, peak_kind = peaks()
-    gemv = gemv_roofline(pkg, peak) if rank == 0 else None
+    # standalone GEMVs of the kernel ABI: both engines at the gate+up and the lm_head shapes
+    gemvs = [gemv_roofline(pkg, peak, engine=e, rows=r) for r in (24576, 248320) for e in ("dp4a", "mma")] \
+        if rank == 0 else None
+    gemv = gemvs[0] if gemvs else None
     step_bytes = info.get("weight_bytes", 0)
     if rank == 0:
         # Algorithmic bytes of one decode step: every weight matrix once (codes + fp16 scales),
@@ -328,6 +339,7 @@ def main():
             "prefill_tok_s": round(prefill_tok_s, 2),
             "roofline": dict(roof, peak_kind=peak_kind),
             "gemv_kernel": dict(gemv, peak_kind=peak_kind) if gemv else None,
+            "gemv_kernels": [dict(g, peak_kind=peak_kind) for g in gemvs] if gemvs else None,
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
                     "api": "xq_decode_one"},
             "gpu_launches": kernels_per_step * args.steps,
