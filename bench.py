@@ -44,18 +44,18 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def package_dir():
+def package_dir(preset="cfg2"):
     base = os.environ.get("XQ_BENCH_DIR", os.path.join(os.environ.get("TMPDIR", "/tmp"), "xq_bench"))
-    return os.path.join(base, f"qwen35_9b_s{SEED}")
+    return os.path.join(base, f"qwen35_9b_s{SEED}" if preset == "cfg2" else f"qwen35_{preset}_s{SEED}")
 
 
-def make_package(rank, world):
+def make_package(rank, world, preset="cfg2"):
     from xqwen35_b200.packer import synthetic
 
-    d = package_dir()
+    d = package_dir(preset)
     if rank == 0:
         t = time.time()
-        synthetic.make_package(d, synthetic.preset("cfg2"), seed=SEED)
+        synthetic.make_package(d, synthetic.preset(preset), seed=SEED)
         print(f"[bench] package ready in {time.time() - t:.1f}s: {d}", file=sys.stderr, flush=True)
     return d
 
@@ -173,7 +173,7 @@ def gemv_roofline(pkg, peak_gbs, iters=40, engine="dp4a", rows=24576, cols=4096)
             "shape": f"{rows}x{cols}", "algorithmic_bytes": alg, "launch_us": round(ms * 1000, 2)}
 
 
-def cpu_baseline(model_dir, steps):
+def cpu_baseline(model_dir, steps, preset="cfg2"):
     """The reference's own CPU path (compiled from its sources) on the same package, on a
     bounded sample: an 8-token prompt then `steps` greedy decode tokens through its C ABI."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -195,8 +195,9 @@ def cpu_baseline(model_dir, steps):
     dt = time.time() - t
     s.close()
     return {"value": round(steps / dt, 4), "unit": "tok/s", "cores": cores, "kind": kind,
-            "sample": f"{steps} greedy decode steps after an 8-token prompt (context 8..{8 + steps}) on the 9B "
-                      f"package; the reference's WorkerPool caps at min(8, hardware_concurrency) threads"}
+            "sample": f"{steps} greedy decode steps after an 8-token prompt (context 8..{8 + steps}) on the "
+                      f"{'9B' if preset == 'cfg2' else preset} package; the reference's WorkerPool caps at "
+                      f"min(8, hardware_concurrency) threads"}
 
 
 def max_over_ranks(x: float, world: int, device: str = "cuda") -> float:
@@ -221,20 +222,21 @@ def run_reference_arm(args, rank, world):
     if rank != 0:
         return 0
     __graft_entry__.load_package()  # registers the package module for the synthetic data generator
-    d = make_package(0, 1)
+    d = make_package(0, 1, args.preset)
     steps = max(1, min(args.steps, 16))
     warm = min(args.warmup, 1)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
     if warm:
-        cpu_baseline(d, warm)
-    cb = cpu_baseline(d, steps)
+        cpu_baseline(d, warm, args.preset)
+    cb = cpu_baseline(d, steps, args.preset)
     line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": steps, "warmup": warm, "ms_per_step": round(1000.0 / cb["value"], 2) if cb["value"] else None,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init package)",
-            "config": {"workload": "config2: Qwen3.5-9B-shaped W4A16 g64, 32 layers, vocab 248320, greedy decode",
+            "config": {"workload": "config2: Qwen3.5-9B-shaped W4A16 g64, 32 layers, vocab 248320, greedy decode"
+                       if args.preset == "cfg2" else f"{args.preset} preset (functional check, not a bench line)",
                        "prompt": 8, "kv_dtype": "f32", "cpu_sample": True},
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -254,6 +256,8 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=12)
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt length (512 = the benchmark shape)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--preset", default="cfg2", choices=["cfg2", "small"],
+                    help="synthetic package: cfg2 = the benchmark's 9B shape; small = a quick functional check")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -270,7 +274,7 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=900))
     pkg = __graft_entry__.load_package()
-    d = make_package(rank, world)
+    d = make_package(rank, world, args.preset)
     if world > 1:
         dist.barrier()
     sess = pkg.Session(d, device=local, kv_fp16=args.kv_fp16, max_context_tokens=args.prompt + args.warmup +
@@ -347,7 +351,9 @@ def main():
             "tokens_head": [int(v) for v in toks[:8]],
         }
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(d, args.cpu_steps)
+            line["cpu_baseline"] = cpu_baseline(d, args.cpu_steps, args.preset)
+        if args.preset != "cfg2":
+            line["config"]["workload"] = f"{args.preset} preset (functional check, not a bench line)"
         print(json.dumps(line), flush=True)
     sess.close()
     if world > 1:
