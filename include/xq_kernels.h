@@ -46,7 +46,8 @@ XQK_API int xqk_gemv_w4a16(const xqk_matrix* m, const float* x_dev, float* y_dev
  * columns, so results agree with it to fp32 rounding, not bit for bit. Served for symmetric
  * version-1 matrices (zero 8) with group 64, fp16-exact scales, cols a multiple of 512 (and
  * of 4096 above 4096), which xqk_matrix_create then also stores in the tensor-core tile
- * layout; other matrices return XQ_ERR_NOT_READY (-2). Finite x only. */
+ * layout; other matrices return XQ_ERR_NOT_READY (-2). A non-finite x makes every row NaN, as
+ * in fp32. */
 XQK_API int xqk_gemv_w4a16_mma(const xqk_matrix* m, const float* x_dev, float* y_dev, void* stream);
 /* The tensor-core tile layout of a symmetric matrix, written to a host buffer (host only, no
  * GPU): no reference counterpart; for packaging pipelines and tests. packed: rows * cols / 2

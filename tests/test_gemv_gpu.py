@@ -149,3 +149,15 @@ def test_tensor_core_gemv_refuses_other_layouts():
     yd = torch.zeros(64, device="cuda")
     with pytest.raises(RuntimeError):
         m.gemv_mma(xd.data_ptr(), yd.data_ptr())
+
+
+def test_tensor_core_gemv_nan_input_propagates():
+    packed, s, z, version, x = seeded(256, 4096, "sym", seed=2)
+    x[17] = np.nan
+    m = PKG.Matrix(packed, s, z, 256, 4096, 64)
+    torch = _torch()
+    xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+    yd = torch.zeros(256, dtype=torch.float32, device="cuda")
+    m.gemv_mma(xd.data_ptr(), yd.data_ptr())
+    torch.cuda.synchronize()
+    assert np.isnan(yd.cpu().numpy()).all()

@@ -114,11 +114,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(const MmaParam
     for (int g = tid; g < p.cols / 64; g += nthr) {
         const float4* xs = reinterpret_cast<const float4*>(p.x + 64 * g);
         float amax = 0.0f;
+        bool finite = true;  // fmaxf drops NaN operands: test every value
         float4 v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             v[i] = __ldg(xs + i);
             amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+            finite = finite && isfinite(v[i].x) && isfinite(v[i].y) && isfinite(v[i].z) && isfinite(v[i].w);
         }
         const int ex = ((__float_as_int(amax) >> 23) & 0xff) - 126;
         const int S = max(-100, min(100, 22 - ex));
@@ -137,7 +139,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(const MmaParam
 #pragma unroll
         for (int d = 0; d < 3; ++d) {
             cinit[pp * 8 + n0 + d] = -8 * zs[d];
-            wtab[pp * 8 + n0 + d] = __int_as_float((127 - S + 8 * d) << 23);  // 256^d * 2^-S
+            // 256^d * 2^-S; NaN for a group holding a non-finite x (every row's result is then NaN,
+            // as in fp32)
+            wtab[pp * 8 + n0 + d] = finite ? __int_as_float((127 - S + 8 * d) << 23) : __int_as_float(0x7fc00000);
         }
         if (g & 1) {
             cinit[pp * 8 + 6] = cinit[pp * 8 + 7] = 0;

@@ -604,11 +604,18 @@ struct XDigits {
 template <int E>
 __device__ __forceinline__ void mma_make_digits(const float (&xv)[E], XDigits<E>& X) {
     float amax = 0.0f;
+    int bad = 0;  // fmaxf drops NaN operands: test every value
 #pragma unroll
-    for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(xv[i]));
+    for (int i = 0; i < E; ++i) {
+        amax = fmaxf(amax, fabsf(xv[i]));
+        bad |= !isfinite(xv[i]);
+    }
 #pragma unroll
-    for (int o = 1; o < 64 / E; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    X.finite = isfinite(amax);
+    for (int o = 1; o < 64 / E; o <<= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, o);
+    }
+    X.finite = !bad;
     // As gemv_make_limbs: amax = f * 2^ex, f in [0.5, 1); m = round_to_nearest_even(x * 2^S)
     // with |m| < 2^22 sits in the low bits of x * 2^S + 1.5 * 2^23, and m + 0x808080 has the
     // digits + 128 as its bytes.
