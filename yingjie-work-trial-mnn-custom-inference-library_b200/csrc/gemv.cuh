@@ -196,65 +196,6 @@ __device__ __forceinline__ void gemv_load_x(const GemvParams& p, int t, int lane
     }
 }
 
-// Prologue from shared memory: the block's copy of x (and, for kProRms, norm_w [cols]; for
-// kProGatedRms, gate_z [cols] followed by norm_w [head_dim]) was brought in by bulk copies.
-// Same arithmetic, in the same order, as gemv_load_x.
-template <int PRO>
-__device__ __forceinline__ void gemv_x_from_smem(const GemvParams& p, const float* xs, const float* vs, int t,
-                                                 int lane, int warp, int team, int wpt, int team_bar, int team_size,
-                                                 float* wsum, float (&xv)[32]) {
-    const float4* src = reinterpret_cast<const float4*>(xs + 32 * t);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float4 a = src[i];
-        xv[4 * i] = a.x;
-        xv[4 * i + 1] = a.y;
-        xv[4 * i + 2] = a.z;
-        xv[4 * i + 3] = a.w;
-    }
-    if constexpr (PRO == kProRms) {
-        // rmsnormReference (ref_rmsnorm.cpp:8-17): x * (1/sqrt(mean(x^2)+eps)) * w
-        float ss = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
-        ss = warp_sum(ss);
-        if (lane == 0) wsum[warp] = ss;
-        named_bar(team_bar, team_size);
-        float tot = 0.0f;
-        for (int w = 0; w < wpt; ++w) tot += wsum[team * wpt + w];
-        const float inv = 1.0f / sqrtf(tot / static_cast<float>(p.cols) + p.eps);
-        const float4* wn = reinterpret_cast<const float4*>(vs + 32 * t);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 g = wn[i];
-            xv[4 * i] = xv[4 * i] * inv * g.x;
-            xv[4 * i + 1] = xv[4 * i + 1] * inv * g.y;
-            xv[4 * i + 2] = xv[4 * i + 2] * inv * g.z;
-            xv[4 * i + 3] = xv[4 * i + 3] * inv * g.w;
-        }
-        named_bar(team_bar, team_size);  // wsum may be reused by the next phase
-    } else if constexpr (PRO == kProGatedRms) {
-        // applyGatedHeadRms (custom_model.cpp:329-349): per head of head_dim columns,
-        // out = in * inv * w * silu(z); head_dim/32 consecutive lanes share one head.
-        float ss = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
-        const int tph = p.head_dim >> 5;
-        for (int o = 1; o < tph; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.head_dim) + p.eps);
-        const float4* gz = reinterpret_cast<const float4*>(vs + 32 * t);
-        const float4* wn = reinterpret_cast<const float4*>(vs + p.cols + (32 * t) % p.head_dim);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 z = gz[i], g = wn[i];
-            xv[4 * i] = xv[4 * i] * inv * g.x * dsilu(z.x);
-            xv[4 * i + 1] = xv[4 * i + 1] * inv * g.y * dsilu(z.y);
-            xv[4 * i + 2] = xv[4 * i + 2] * inv * g.z * dsilu(z.z);
-            xv[4 * i + 3] = xv[4 * i + 3] * inv * g.w * dsilu(z.w);
-        }
-    }
-}
-
 template <int META>
 __device__ __forceinline__ void gemv_make_limbs(const float (&xv)[32], XLimbs& L) {
     float amax = 0.0f, xsum = 0.0f;

@@ -306,7 +306,8 @@ __device__ __forceinline__ void gated_prologue(const GemvParams& p, Ctx& c) {
     named_bar(1, kStepConsumers);  // the normalised x is visible to every team; wsum free again
 }
 
-// gemv_load_x's arithmetic on the staged copies (same operations in the same order).
+// gemv_load_x's arithmetic on the staged copies (same operations in the same order); a gated
+// prologue has normalised x in place already (gated_prologue).
 template <int PRO>
 __device__ __forceinline__ void staged_prologue(const GemvParams& p, const float* act, int t, int lane, int warp,
                                                 int team, int wpt, int team_bar, int team_size, float* wsum,
@@ -328,27 +329,6 @@ __device__ __forceinline__ void staged_prologue(const GemvParams& p, const float
 #pragma unroll
         for (int i = 0; i < 32; ++i) xv[i] = xv[i] * inv * g[i];
         named_bar(team_bar, team_size);  // wsum may be reused by the next phase
-    } else if constexpr (PRO == kProGatedRms) {
-        // applyGatedHeadRms (custom_model.cpp:329-349): per head of head_dim columns,
-        // out = in * inv * w * silu(z); head_dim/32 consecutive lanes share one head.
-        float ss = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
-        const int tph = p.head_dim >> 5;
-        for (int o = 1; o < tph; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float inv = 1.0f / sqrtf(ss / static_cast<float>(p.head_dim) + p.eps);
-        float z[32];
-        staged_row(act + p.cols, t, z);
-        const float* wn = act + 2 * p.cols;
-        const int wr = t % tph;  // row of the staged head_dim weights
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float4 g = *reinterpret_cast<const float4*>(wn + 32 * wr + 4 * (i ^ (wr & 7)));
-            xv[4 * i] = xv[4 * i] * inv * g.x * dsilu(z[4 * i]);
-            xv[4 * i + 1] = xv[4 * i + 1] * inv * g.y * dsilu(z[4 * i + 1]);
-            xv[4 * i + 2] = xv[4 * i + 2] * inv * g.z * dsilu(z[4 * i + 2]);
-            xv[4 * i + 3] = xv[4 * i + 3] * inv * g.w * dsilu(z[4 * i + 3]);
-        }
     }
 }
 
