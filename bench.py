@@ -18,7 +18,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import re
 import subprocess
 import sys
 import threading
@@ -109,13 +108,28 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
-def profile_figure(name, key):
-    """A per-launch figure recorded in a committed ncu summary under profiles/ (or None)."""
-    path = os.path.join(ROOT, "profiles", name)
-    if not os.path.exists(path):
+def ncu_traffic(kernel):
+    """DRAM read + write bytes per launch of `kernel` from one ncu capture, kept as a figure in
+    profiles/ncu_traffic.json (the capture command is recorded beside it); None if absent."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            e = json.load(f).get(kernel)
+        return {"bytes": e["traffic_bytes_per_launch"], "source": e["source"]} if e else None
+    except Exception:
         return None
-    m = re.search(key + r":\s*([0-9.]+)", open(path).read())
-    return float(m.group(1)) if m else None
+
+
+def host_cpu():
+    """The host's CPU model and core count, recorded next to every CPU-timed number."""
+    model = None
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except Exception:
+        pass
+    return {"cpu_model": model, "nproc": os.cpu_count()}
 
 
 def step_roofline(alg_bytes, ms_per_step, peak_gbs):
@@ -123,9 +137,10 @@ def step_roofline(alg_bytes, ms_per_step, peak_gbs):
     phase of the step inside it). achieved = algorithmic bytes of one step / the mean launch
     duration from CUDA events on the session stream over the timed region."""
     achieved = alg_bytes / (ms_per_step * 1e-3) / 1e9
+    tr = ncu_traffic("decode_step_kernel")
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
-            "frac": round(achieved / peak_gbs, 4),
-            "traffic": profile_figure("decode_step_kernel_9b.md", "traffic_bytes_per_launch"),
+            "frac": round(achieved / peak_gbs, 4), "traffic": tr["bytes"] if tr else None,
+            "traffic_source": tr["source"] if tr else None,
             "kernel": "decode_step_kernel", "algorithmic_bytes": int(alg_bytes),
             "launch_us": round(ms_per_step * 1000, 2)}
 
@@ -173,14 +188,107 @@ def gemv_roofline(pkg, peak_gbs, iters=40, engine="dp4a", rows=24576, cols=4096)
             "shape": f"{rows}x{cols}", "algorithmic_bytes": alg, "launch_us": round(ms * 1000, 2)}
 
 
-def cpu_baseline(model_dir, steps, preset="cfg2"):
-    """The reference's own CPU path (compiled from its sources) on the same package, on a
-    bounded sample: an 8-token prompt then `steps` greedy decode tokens through its C ABI."""
+def config0_gemv(pkg, peak_gbs, iters=200):
+    """Config 0 as specified: one W4A16 g64 GEMV, W [12288 x 4096] symmetric int4, x fp16
+    ~ N(0, 1), y fp16, fp32 accumulation, through xqk_gemv_w4a16_mma_f16. Launched back to back
+    over 8 weight copies (214 MB > L2), as a GEMV chain in a stream runs: each launch streams
+    its own copy from HBM. Algorithmic bytes N*K/2 + N*(K/64)*2 + 2K + 2N = 26,771,456 per call.
+    e2e: the same call with x in pinned host memory copied in and y copied out every call."""
+    import torch
+
+    rows, cols = 12288, 4096
+    ncopy = 8
+    mats = []
+    for i in range(ncopy):
+        rng = np.random.default_rng(300 + i)
+        packed = rng.integers(0, 256, rows * cols // 2, dtype=np.uint8)
+        sc = (np.abs(rng.standard_normal(rows * cols // 64)) * 0.02).astype(np.float16).astype(np.float32)
+        mats.append(pkg.Matrix(packed, sc, np.full(rows * cols // 64, 8.0, np.float32), rows, cols, 64))
+    x = torch.randn(cols, device="cuda").half()
+    y = torch.zeros(rows, device="cuda", dtype=torch.float16)
+    st = torch.cuda.current_stream()
+    for m in mats:
+        m.gemv_mma_f16(x.data_ptr(), y.data_ptr(), st.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(iters):
+        mats[i % ncopy].gemv_mma_f16(x.data_ptr(), y.data_ptr(), st.cuda_stream)
+    e1.record(st)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / iters * 1000
+    alg = rows * cols // 2 + rows * (cols // 64) * 2 + 2 * cols + 2 * rows
+    achieved = alg / (us * 1e-6) / 1e9
+    # e2e through the kernel ABI with host buffers: pinned x in, y out, every call
+    xh = torch.randn(cols).half().pin_memory()
+    yh = torch.zeros(rows, dtype=torch.float16).pin_memory()
+    n_e2e = 100
+    for i in range(3):
+        x.copy_(xh, non_blocking=True)
+        mats[i % ncopy].gemv_mma_f16(x.data_ptr(), y.data_ptr(), st.cuda_stream)
+        yh.copy_(y, non_blocking=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(n_e2e):
+        x.copy_(xh, non_blocking=True)
+        mats[i % ncopy].gemv_mma_f16(x.data_ptr(), y.data_ptr(), st.cuda_stream)
+        yh.copy_(y, non_blocking=True)
+        st.synchronize()
+    e2e_us = (time.perf_counter() - t0) / n_e2e * 1e6
+    for m in mats:
+        m.close()
+    return {"workload": "config0: W4A16 g64 GEMV 12288x4096, x/y fp16, fp32 accumulate, batch 1",
+            "kernel": "gemv_mma_kernel<half, half>", "metric": "GEMV HBM GB/s", "value": round(achieved, 1),
+            "unit": "GB/s", "us_per_call": round(us, 3), "algorithmic_bytes": alg,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+                         "frac": round(achieved / peak_gbs, 4)},
+            "l2": "8 weight copies (214 MB) rotated, each launch reads its copy from HBM",
+            "launch": "back to back, programmatic dependent launch",
+            "e2e": {"us_per_call": round(e2e_us, 2), "h2d_bytes_per_call": 2 * cols, "d2h_bytes_per_call": 2 * rows,
+                    "api": "xqk_gemv_w4a16_mma_f16 with pinned host x / y copied every call"}}
+
+
+def config1_step(pkg, peak_gbs, kv_fp16, steps=64):
+    """Config 1: one decode step through two random-init 9B-shaped layers (DeltaNet + full
+    attention) with the KV cache at 512 tokens: a 512-token prefill, then `steps` timed greedy
+    steps (persistent step kernel, CUDA events on the session stream). The 234 MB of weights
+    exceed L2. Algorithmic bytes per step: both layers' matrices and the lm_head (codes + fp16
+    scales), the DeltaNet recurrent and conv states read and written, the KV cache read at the
+    mean timed context and one row written, the embedding row."""
+    d = package_dir("cfg1")
+    from xqwen35_b200.packer import synthetic
+
+    synthetic.make_package(d, synthetic.preset("cfg1"), seed=SEED)
+    s = pkg.Session(d, device=0, kv_fp16=kv_fp16, max_context_tokens=512 + steps + 64)
+    ids = np.random.default_rng(SEED + 1).integers(0, 1024, 512).astype(np.int32)
+    s.prefill(ids)
+    s.decode_timed(4)
+    ms, _ = s.decode_timed(steps)
+    info = json.loads(s.json("backend"))
+    s.close()
+    us = ms / steps * 1000
+    kv_elem = 2 if kv_fp16 else 4
+    ctx = 512 + 4 + steps / 2
+    alg = (info.get("weight_bytes", 0) + 2 * 32 * 128 * 128 * 4 + 2 * 8192 * 3 * 4 +
+           2 * 4 * 256 * kv_elem * (ctx + 1) + 4096 * 2)
+    achieved = alg / (us * 1e-6) / 1e9
+    return {"workload": "config1: 2 layers (Gated-DeltaNet + GQA) at 9B shapes, vocab 1024, KV cache 512",
+            "kernel": "decode_step_kernel", "us_per_step": round(us, 2), "algorithmic_bytes": int(alg),
+            "kv_dtype": "f16" if kv_fp16 else "f32",
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+                         "frac": round(achieved / peak_gbs, 4)},
+            "l2": "inputs larger than L2 (234 MB of weights streamed per step)"}
+
+
+def cpu_baseline(model_dir, steps, preset="cfg2", prompt=PROMPT_LEN):
+    """The reference's own CPU path (compiled from its sources) on the same package and context,
+    on a bounded sample: a `prompt`-token prefill (untimed), then `steps` greedy decode tokens
+    through its C ABI, timed."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
     cores = min(8, os.cpu_count() or 1)
-    ids = np.random.default_rng(SEED).integers(0, 248320, 8).astype(np.int32)
+    ids = np.random.default_rng(SEED).integers(0, 248320, prompt).astype(np.int32)
     if oracle.ref_available():
         s = oracle.RefSession(model_dir, threads=cores)
         kind = "reference"
@@ -194,10 +302,10 @@ def cpu_baseline(model_dir, steps, preset="cfg2"):
         s.decode_one()
     dt = time.time() - t
     s.close()
-    return {"value": round(steps / dt, 4), "unit": "tok/s", "cores": cores, "kind": kind,
-            "sample": f"{steps} greedy decode steps after an 8-token prompt (context 8..{8 + steps}) on the "
-                      f"{'9B' if preset == 'cfg2' else preset} package; the reference's WorkerPool caps at "
-                      f"min(8, hardware_concurrency) threads"}
+    return dict({"value": round(steps / dt, 4), "unit": "tok/s", "cores": cores, "kind": kind,
+                 "sample": f"{steps} greedy decode steps after a {prompt}-token prompt (context {prompt}.."
+                           f"{prompt + steps}) on the {'9B' if preset == 'cfg2' else preset} package; the "
+                           f"reference's WorkerPool caps at min(8, hardware_concurrency) threads"}, **host_cpu())
 
 
 def max_over_ranks(x: float, world: int, device: str = "cuda") -> float:
@@ -224,20 +332,19 @@ def run_reference_arm(args, rank, world):
     __graft_entry__.load_package()  # registers the package module for the synthetic data generator
     d = make_package(0, 1, args.preset)
     steps = max(1, min(args.steps, 16))
-    warm = min(args.warmup, 1)
+    warm = 0  # the untimed 512-token prefill warms the reference's caches and thread pool
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
-    if warm:
-        cpu_baseline(d, warm, args.preset)
-    cb = cpu_baseline(d, steps, args.preset)
+    prompt = min(args.prompt, PROMPT_LEN)
+    cb = cpu_baseline(d, steps, args.preset, prompt=prompt)
     line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": steps, "warmup": warm, "ms_per_step": round(1000.0 / cb["value"], 2) if cb["value"] else None,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random-init package)",
             "config": {"workload": "config2: Qwen3.5-9B-shaped W4A16 g64, 32 layers, vocab 248320, greedy decode"
                        if args.preset == "cfg2" else f"{args.preset} preset (functional check, not a bench line)",
-                       "prompt": 8, "kv_dtype": "f32", "cpu_sample": True},
+                       "prompt": prompt, "kv_dtype": "f32", "cpu_sample": True},
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if not oracle.ref_available():
@@ -256,6 +363,7 @@ def main():
     ap.add_argument("--cpu-steps", type=int, default=12)
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt length (512 = the benchmark shape)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the config-0 GEMV and config-1 step lines")
     ap.add_argument("--preset", default="cfg2", choices=["cfg2", "small"],
                     help="synthetic package: cfg2 = the benchmark's 9B shape; small = a quick functional check")
     args = ap.parse_args()
@@ -313,6 +421,8 @@ def main():
     gemvs = [gemv_roofline(pkg, peak, engine=e, rows=r) for r in (24576, 248320) for e in ("dp4a", "mma")] \
         if rank == 0 else None
     gemv = gemvs[0] if gemvs else None
+    cfg0 = config0_gemv(pkg, peak) if rank == 0 and not args.no_extra else None
+    cfg1 = config1_step(pkg, peak, args.kv_fp16) if rank == 0 and not args.no_extra else None
     step_bytes = info.get("weight_bytes", 0)
     if rank == 0:
         # Algorithmic bytes of one decode step: every weight matrix once (codes + fp16 scales),
@@ -344,6 +454,8 @@ def main():
             "roofline": dict(roof, peak_kind=peak_kind),
             "gemv_kernel": dict(gemv, peak_kind=peak_kind) if gemv else None,
             "gemv_kernels": [dict(g, peak_kind=peak_kind) for g in gemvs] if gemvs else None,
+            "config0_gemv": cfg0,
+            "config1_step": cfg1,
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
                     "api": "xq_decode_one"},
             "gpu_launches": kernels_per_step * args.steps,
@@ -351,7 +463,7 @@ def main():
             "tokens_head": [int(v) for v in toks[:8]],
         }
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(d, args.cpu_steps, args.preset)
+            line["cpu_baseline"] = cpu_baseline(d, args.cpu_steps, args.preset, prompt=args.prompt)
         if args.preset != "cfg2":
             line["config"]["workload"] = f"{args.preset} preset (functional check, not a bench line)"
         print(json.dumps(line), flush=True)

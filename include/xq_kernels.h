@@ -49,6 +49,13 @@ XQK_API int xqk_gemv_w4a16(const xqk_matrix* m, const float* x_dev, float* y_dev
  * layout; other matrices return XQ_ERR_NOT_READY (-2). A non-finite x makes every row NaN, as
  * in fp32. */
 XQK_API int xqk_gemv_w4a16_mma(const xqk_matrix* m, const float* x_dev, float* y_dev, void* stream);
+/* xqk_gemv_w4a16_mma with fp16 activations: x and y are fp16 device vectors (x 8-byte
+ * aligned), the arithmetic is the same exact-integer / fp32 path and y is rounded to fp16 once.
+ * The benchmark's single-GEMV configuration (x fp16 [4096], y fp16, fp32 accumulate) in its own
+ * format; the reference kernel takes fp32 vectors (gemvW4A16Neon, xq_gemv_w4a16_neon.cpp:259).
+ * Both tensor-core GEMVs launch with programmatic dependent launch: the weight stream may start
+ * while the previous kernel in the stream finishes, x is read only after it has finished. */
+XQK_API int xqk_gemv_w4a16_mma_f16(const xqk_matrix* m, const void* x_dev, void* y_dev, void* stream);
 /* The tensor-core tile layout of a symmetric matrix, written to a host buffer (host only, no
  * GPU): no reference counterpart; for packaging pipelines and tests. packed: rows * cols / 2
  * bytes in the reference's nibble order, scales: rows * cols / 64 fp32 (zero 8 implied, scales

@@ -4,7 +4,8 @@
  * entry point below has the same name, layout and meaning as xqwen35.h:19-77 of the
  * reference, so a host that compiled against that header links against this library
  * unchanged. The work behind it runs on an NVIDIA B200 (sm_100a): weights, KV cache and
- * recurrent state live in HBM and each decode step is one CUDA graph.
+ * recurrent state live in HBM and each decode step is one launch of a persistent cooperative
+ * kernel (shapes that kernel does not take run the step as a CUDA graph of per-op kernels).
  *
  * Additions (not in the reference): xq_cuda_options + xq_create_cuda, to pick the device
  * and KV-cache precision; everything else is the reference interface.

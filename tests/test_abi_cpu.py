@@ -21,10 +21,13 @@ def declared_functions():
 
 
 def test_library_built_for_sm100a():
+    """The build compiles every CUDA source for sm_100a only (checked on the build recipe; the
+    GPU test test_step_kernel_binary_is_sm100 checks the loaded kernel's binary version)."""
     assert os.path.exists(PKG.LIB_PATH), "run __graft_entry__.build()"
-    with open(PKG.LIB_PATH, "rb") as f:
-        blob = f.read()
-    assert b"sm_100a" in blob or b"sm_100" in blob
+    mk = open(os.path.join(PKG.CSRC, "Makefile")).read()
+    arch = re.search(r"^ARCH\s*:=\s*(.*)$", mk, re.M).group(1).split()
+    assert arch == ["-gencode", "arch=compute_100a,code=sm_100a"]
+    assert "$(ARCH)" in re.search(r"^NVFLAGS\s*:=.*$", mk, re.M).group(0)
 
 
 def test_exports_every_declared_symbol():

@@ -161,3 +161,25 @@ def test_tensor_core_gemv_nan_input_propagates():
     m.gemv_mma(xd.data_ptr(), yd.data_ptr())
     torch.cuda.synchronize()
     assert np.isnan(yd.cpu().numpy()).all()
+
+
+def test_config0_fp16_gemv_vs_oracle(oracle):
+    """Config 0 as specified: W [12288 x 4096] int4 g64 symmetric, x fp16 ~ N(0, 1), y fp16 with
+    fp32 accumulation. The oracle runs the reference algorithm in fp32 on the same fp16 x; the
+    only extra error is y's final rounding to fp16 (relative 2^-11 per element), so the bar is
+    the fp32 bar plus that rounding: |y - y_ref| <= 1e-5 * max|y_ref| + 2^-11 * |y_ref|."""
+    torch = _torch()
+    rows, cols = 12288, 4096
+    packed, s, z, version, _ = seeded(rows, cols, "sym", seed=12288)
+    x16 = np.random.default_rng(0).standard_normal(cols).astype(np.float16)
+    m = PKG.Matrix(packed, s, z, rows, cols, 64, version)
+    ref = oracle.port_gemv(oracle.Matrix(rows, cols, 64, version, packed, s, z), x16.astype(np.float32))
+    xd = torch.from_numpy(x16).cuda()
+    for _ in range(2):  # twice: the second launch overlaps nothing but must agree as well
+        yd = torch.full((rows,), float("nan"), dtype=torch.float16, device="cuda")
+        m.gemv_mma_f16(xd.data_ptr(), yd.data_ptr())
+        torch.cuda.synchronize()
+        y = yd.cpu().numpy().astype(np.float32)
+        assert np.all(np.isfinite(y))
+        bound = 1e-5 * np.abs(ref).max() + 2.0 ** -11 * np.abs(ref)
+        assert np.all(np.abs(y - ref) <= bound)

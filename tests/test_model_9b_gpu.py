@@ -29,3 +29,75 @@ def test_9b_package_matches_reference_golden():
         assert rel_err(s.hidden(), G["hidden_after"]) <= 1e-4
     finally:
         s.close()
+
+
+def topk_from_debug(s):
+    import json
+
+    t = json.loads(s.json("debug"))["lm_head_topk"]
+    return np.array([e["logit"] for e in t], np.float64), np.array([e["token"] for e in t], np.int64)
+
+
+def check_topk(s, want_v, want_i, tol=1e-4):
+    """Top-10 lm_head logits of the session (xq_get_debug_json, the reference's debugJson schema)
+    against the reference's: values within `tol` of the largest, indices exactly where the
+    reference's own neighbouring logits are further apart than the tolerance (a closer pair may
+    swap under fp32 summation-order differences)."""
+    v, i = topk_from_debug(s)
+    scale = np.abs(want_v).max()
+    assert np.abs(v - want_v).max() <= tol * scale
+    sep = np.abs(np.diff(want_v.astype(np.float64))) > 2 * tol * scale
+    n = len(want_i)
+    for k in range(n - 1):  # the last one's lower neighbour (11th) is not recorded
+        if (k == 0 or sep[k - 1]) and sep[k]:
+            assert i[k] == want_i[k], (k, i, want_i)
+
+
+def run_checkpointed(d, G, kv_fp16=False, hid_tol=1e-4, logit_tol=1e-4):
+    s = PKG.Session(d, device=0, kv_fp16=kv_fp16)
+    try:
+        s.prefill(G["ids"])
+        steps = list(G["steps"])
+        assert steps[0] == 0
+        assert rel_err(s.hidden(), G["hidden"][0]) <= hid_tol
+        check_topk(s, G["topk_values"][0], G["topk_indices"][0], logit_tol)
+        toks = []
+        for k in range(1, len(G["tokens"]) + 1):
+            toks.append(s.decode_one())
+            if k in steps:
+                j = steps.index(k)
+                assert rel_err(s.hidden(), G["hidden"][j]) <= hid_tol, k
+                check_topk(s, G["topk_values"][j], G["topk_indices"][j], logit_tol)
+        assert toks == list(G["tokens"])
+    finally:
+        s.close()
+
+
+P512 = os.path.join(GOLDEN, "model_9b_p512_s2024.npz")
+CFG1_512 = os.path.join(GOLDEN, "model_cfg1_p512_s2024.npz")
+
+
+@pytest.mark.skipif(not os.path.exists(P512), reason="9B 512-token golden file not generated")
+def test_9b_benchmark_shape_matches_reference_golden():
+    """The benchmark shape: a 512-token prompt, then 32 greedy steps. After prefill and after
+    steps 1, 8 and 32: the hidden state within 1e-4 and the top-10 logits (values within 1e-4,
+    indices exact) of the reference, and all 32 tokens exactly."""
+    d = os.path.join(os.environ.get("XQ_BENCH_DIR", os.path.join(os.environ.get("TMPDIR", "/tmp"), "xq_bench")),
+                     "qwen35_9b_s2024")
+    synthetic.make_package(d, synthetic.preset("cfg2"), seed=2024)
+    run_checkpointed(d, np.load(P512))
+
+
+@pytest.mark.skipif(not os.path.exists(CFG1_512), reason="cfg1 512-token golden file not generated")
+@pytest.mark.parametrize("kv_fp16", [False, True])
+def test_cfg1_kv512_matches_reference_golden(kv_fp16):
+    """Config 1 (two 9B-shaped layers, vocab 1024) with the KV cache filled to 512 by prefill,
+    then 8 decode steps, against the reference: fp32 KV within 1e-4 (hidden and logits); fp16 KV
+    (the build's cache type) within 5e-3 and 2e-3."""
+    d = os.path.join(os.environ.get("XQ_BENCH_DIR", os.path.join(os.environ.get("TMPDIR", "/tmp"), "xq_bench")),
+                     "qwen35_cfg1_s2024")
+    synthetic.make_package(d, synthetic.preset("cfg1"), seed=2024)
+    if kv_fp16:
+        run_checkpointed(d, np.load(CFG1_512), kv_fp16=True, hid_tol=5e-3, logit_tol=2e-3)
+    else:
+        run_checkpointed(d, np.load(CFG1_512))

@@ -158,3 +158,9 @@ def test_cfg1_two_layer_decode_step(oracle):
     toks = [s.decode_one() for _ in range(2)]
     assert toks == [p.decode_one() for _ in range(2)]
     assert rel_err(s.hidden(), p.hidden()) <= 1e-4
+
+
+def test_step_kernel_binary_is_sm100(small_session):
+    """The loaded persistent step kernel was compiled for sm_100a (cudaFuncGetAttributes)."""
+    info = json.loads(small_session.json("backend"))
+    assert info["step_kernel_binary_version"] == 100

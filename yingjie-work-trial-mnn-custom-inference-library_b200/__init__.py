@@ -36,7 +36,7 @@ KERNEL_SYMBOLS = [
     "xqk_last_error", "xqk_matrix_create", "xqk_matrix_destroy", "xqk_matrix_info", "xqk_gemv_w4a16",
     "xqk_gemv_w4a16_host", "xqk_gemv_w4a16_argmax", "xqk_rmsnorm", "xqk_gated_delta_step",
     "xqk_attention_step", "xqk_attention_step_noalloc", "xqk_gemv_w4a16_mma",
-    "xqk_mma_tiles",
+    "xqk_mma_tiles", "xqk_gemv_w4a16_mma_f16",
 ]
 
 
@@ -105,6 +105,7 @@ def lib():
                                   C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int)]
     L.xqk_gemv_w4a16.argtypes = [P, P, P, P]
     L.xqk_gemv_w4a16_mma.argtypes = [P, P, P, P]
+    L.xqk_gemv_w4a16_mma_f16.argtypes = [P, P, P, P]
     L.xqk_mma_tiles.argtypes = [P, P, C.c_int, C.c_int, P, C.c_size_t, C.POINTER(C.c_size_t)]
     L.xqk_gemv_w4a16_host.argtypes = [P, P, P]
     L.xqk_gemv_w4a16_argmax.argtypes = [P, P, P, P, P]
@@ -162,6 +163,10 @@ class Matrix:
         """y = W x on the integer tensor cores (xqk_gemv_w4a16_mma)."""
         check(lib().xqk_gemv_w4a16_mma(self.h, x_ptr, y_ptr, stream or None), "xqk_gemv_w4a16_mma")
 
+    def gemv_mma_f16(self, x_ptr: int, y_ptr: int, stream: int = 0) -> None:
+        """y = W x with fp16 x and y on the integer tensor cores (xqk_gemv_w4a16_mma_f16)."""
+        check(lib().xqk_gemv_w4a16_mma_f16(self.h, x_ptr, y_ptr, stream or None), "xqk_gemv_w4a16_mma_f16")
+
     def gemv_host(self, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, np.float32)
         y = np.zeros(self.rows, np.float32)
@@ -206,7 +211,8 @@ class Session:
         self.h = C.c_void_p()
         st = L.xq_create_cuda(model_dir.encode(), C.byref(o), C.byref(co), C.byref(self.h))
         if st != XQ_OK:
-            raise RuntimeError(f"xq_create_cuda failed: {st}")
+            self.status = st
+            raise RuntimeError(f"xq_create_cuda failed: {st} {last_error()}")
 
     def _m(self):
         m = XqMetrics()

@@ -624,8 +624,26 @@ int xqk_gemv_w4a16_mma(const xqk_matrix* m, const float* x_dev, float* y_dev, vo
                             "group 64, fp16-exact scales, cols a multiple of 512 and of 4096 above 4096)");
         return -2;
     }
-    return xqb::launch_mma_gemv(m->mma, x_dev, y_dev, m->err, m->num_sms, static_cast<cudaStream_t>(stream)) ? 0
-                                                                                                              : -4;
+    return xqb::launch_mma_gemv(m->mma, x_dev, y_dev, m->err, m->num_sms, static_cast<cudaStream_t>(stream), true)
+               ? 0
+               : -4;
+}
+
+int xqk_gemv_w4a16_mma_f16(const xqk_matrix* m, const void* x_dev, void* y_dev, void* stream) {
+    if (!m || !x_dev || !y_dev) return -1;
+    if (!m->mma.d_tiles) {
+        xqb::set_last_error("xqk_gemv_w4a16_mma_f16: matrix not in the tensor-core layout (needs symmetric xq4 v1, "
+                            "group 64, fp16-exact scales, cols a multiple of 512 and of 4096 above 4096)");
+        return -2;
+    }
+    if ((reinterpret_cast<uintptr_t>(x_dev) & 7u) != 0) {
+        xqb::set_last_error("xqk_gemv_w4a16_mma_f16: x must be 8-byte aligned");
+        return -1;
+    }
+    return xqb::launch_mma_gemv_f16(m->mma, static_cast<const __half*>(x_dev), static_cast<__half*>(y_dev), m->err,
+                                    m->num_sms, static_cast<cudaStream_t>(stream), true)
+               ? 0
+               : -4;
 }
 
 int xqk_mma_tiles(const uint8_t* packed, const float* scales, int rows, int cols, uint8_t* out, size_t capacity,

@@ -34,10 +34,11 @@ constexpr int kMmaConsumerWarps = kMmaTeams * kMmaWarpsPerTeam;
 constexpr int kMmaThreads = 32 * (kMmaConsumerWarps + 1);
 constexpr int kMmaMaxSlots = 8;
 
+template <typename XT, typename YT>
 struct MmaParams {
     const uint8_t* tiles;
-    const float* x;
-    float* y;
+    const XT* x;
+    YT* y;
     int rows, cols, ntiles, pairs;
     int ppc;  // group pairs per ring chunk
     int cpt;  // chunks per tile
@@ -61,7 +62,23 @@ __device__ __forceinline__ uint32_t digit_byte(float x, float up, int d) {
     return ((u >> (8 * d)) & 0xffu) ^ 0x80u;
 }
 
-__global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(const MmaParams p) {
+// Four consecutive x values as fp32 (x is fp32 or fp16; 16- or 8-byte aligned by construction).
+__device__ __forceinline__ float4 load_x4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 load_x4(const __half* p) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void store_y(float* y, float v) { *y = v; }
+__device__ __forceinline__ void store_y(__half* y, float v) { *y = __float2half_rn(v); }
+
+// The weight stream does not depend on any earlier kernel: with programmatic dependent launch
+// the producer starts streaming while the previous kernel in the stream finishes, and the
+// consumers wait for it (griddepcontrol.wait) before reading x. Without the launch attribute
+// the wait returns at once.
+template <typename XT, typename YT>
+__global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(const MmaParams<XT, YT> p) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffFull);
     uint64_t* empty = reinterpret_cast<uint64_t*>(smem + kOffEmpty);
@@ -86,6 +103,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(const MmaParam
         fence_mbar_init();
     }
     __syncthreads();
+    pdl_launch_dependents();
 
     if (warp == kMmaConsumerWarps) {  // producer: this block's tiles, chunk by chunk
         if (lane == 0) {
@@ -110,15 +128,15 @@ __global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(const MmaParam
     }
 
     // ---- prologue: group exponents, zero-point start values, column weights, B fragments ----
+    pdl_wait();  // x may be the previous kernel's output
     constexpr int nthr = kMmaConsumerWarps * 32;
     for (int g = tid; g < p.cols / 64; g += nthr) {
-        const float4* xs = reinterpret_cast<const float4*>(p.x + 64 * g);
         float amax = 0.0f;
         bool finite = true;  // fmaxf drops NaN operands: test every value
         float4 v[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            v[i] = __ldg(xs + i);
+            v[i] = load_x4(p.x + 64 * g + 4 * i);
             amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
             finite = finite && isfinite(v[i].x) && isfinite(v[i].y) && isfinite(v[i].z) && isfinite(v[i].w);
         }
@@ -158,8 +176,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(const MmaParam
             const int d = n % 3, g = 2 * (slab >> 2) + (s >= 2 ? 1 : 0);
             const float up = __int_as_float((sexp[g] + 127) << 23);
             const int k0 = 32 * slab + (L & 3) * 4;
-            const float4 lo = __ldg(reinterpret_cast<const float4*>(p.x + k0));
-            const float4 hi = __ldg(reinterpret_cast<const float4*>(p.x + k0 + 16));
+            const float4 lo = load_x4(p.x + k0);
+            const float4 hi = load_x4(p.x + k0 + 16);
             b.x = digit_byte(lo.x, up, d) | (digit_byte(lo.y, up, d) << 8) | (digit_byte(lo.z, up, d) << 16) |
                   (digit_byte(lo.w, up, d) << 24);
             b.y = digit_byte(hi.x, up, d) | (digit_byte(hi.y, up, d) << 8) | (digit_byte(hi.z, up, d) << 16) |
@@ -218,7 +236,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) gemv_mma_kernel(const MmaParam
             const float* t0 = red + tau * kMmaWarpsPerTeam * 16;
             const float yv = (t0[lane] + t0[16 + lane]) + (t0[32 + lane] + t0[48 + lane]);
             const int row = tile * 16 + lane;
-            if (row < p.rows) p.y[row] = yv;
+            if (row < p.rows) store_y(p.y + row, yv);
         }
         named_bar(2 + tau, 32 * kMmaWarpsPerTeam);
     }
@@ -376,12 +394,17 @@ void free_mma_matrix(MmaMatrix* m) {
 }
 
 bool mma_init_device() {
-    XQB_CUDA_OK(cudaFuncSetAttribute(gemv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    XQB_CUDA_OK(cudaFuncSetAttribute(gemv_mma_kernel<float, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     227 * 1024));
+    XQB_CUDA_OK(cudaFuncSetAttribute(gemv_mma_kernel<__half, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     227 * 1024));
     return true;
 }
 
-bool launch_mma_gemv(const MmaMatrix& m, const float* x, float* y, unsigned* err, int num_sms, cudaStream_t s) {
-    MmaParams p = {};
+namespace {
+template <typename XT, typename YT>
+bool launch_mma_gemv_t(const MmaMatrix& m, const XT* x, YT* y, unsigned* err, int num_sms, cudaStream_t s, bool pdl) {
+    MmaParams<XT, YT> p = {};
     p.tiles = m.d_tiles;
     p.x = x;
     p.y = y;
@@ -402,13 +425,33 @@ bool launch_mma_gemv(const MmaMatrix& m, const float* x, float* y, unsigned* err
     }
     const size_t smem = fixed + slot * p.nslots;
     const int grid = std::max(1, std::min(num_sms, m.ntiles));
-    gemv_mma_kernel<<<grid, kMmaThreads, smem, s>>>(p);
-    const cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kMmaThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_mma_kernel<XT, YT>, p);
     if (e != cudaSuccess) {
         set_last_error(std::string("tensor-core GEMV launch failed: ") + cudaGetErrorString(e));
         return false;
     }
     return true;
+}
+}  // namespace
+
+bool launch_mma_gemv(const MmaMatrix& m, const float* x, float* y, unsigned* err, int num_sms, cudaStream_t s,
+                     bool pdl) {
+    return launch_mma_gemv_t(m, x, y, err, num_sms, s, pdl);
+}
+
+bool launch_mma_gemv_f16(const MmaMatrix& m, const __half* x, __half* y, unsigned* err, int num_sms, cudaStream_t s,
+                         bool pdl) {
+    return launch_mma_gemv_t(m, x, y, err, num_sms, s, pdl);
 }
 
 }  // namespace xqb

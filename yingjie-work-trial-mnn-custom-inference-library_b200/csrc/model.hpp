@@ -93,6 +93,11 @@ public:
     bool restore_snapshot(const void* buf, size_t size, std::string* error, bool* invalid);
     // Device error word set by bounded waits; 0 when clean.
     unsigned device_errors();
+    // Zero the error word and the step kernel's barrier and merge counters (session stream).
+    void clear_device_errors();
+    // false (with a message) when the error word is set after `what`; the word is then cleared
+    // so that xq_reset and later steps start clean.
+    bool check_device_errors(const char* what, std::string* error);
 
     const ModelDims& dims() const { return d_; }
     size_t weight_bytes() const { return weight_bytes_; }
@@ -154,6 +159,7 @@ private:
     unsigned* d_attn_counters_ = nullptr;
     unsigned* d_err_ = nullptr;
     int32_t* h_token_ = nullptr;  // pinned
+    unsigned* h_err_ = nullptr;   // pinned
     int ring_cap_ = 1 << 16;
 
     cudaStream_t stream_ = nullptr;
@@ -173,6 +179,9 @@ private:
     int step_inflight_ = 0;
     int step_l2_prefetch_ = 1;
     int step_l2_ahead_ = 0;  // chunks (XQ_STEP_L2_AHEAD); prefetching into L2 measured slower
+    unsigned long long step_wait_ns_ = 0;  // 0: the kernels' default limit (2 s)
+    long long stall_launch_ = -1;          // failure-detection test hook (XQ_TEST_STALL_LAUNCH)
+    long long step_launches_ = 0;          // step-kernel launches since load
     PhaseDesc* d_phases_decode_ = nullptr;
     void* d_tmaps_ = nullptr;  // CUtensorMap array of the phase lists
     bool packed_layout_ = false;  // weights read from b200/*.b200

@@ -168,10 +168,16 @@ int xqk_attention_step(const float* qkv_dev, const float* q_norm_dev, const floa
     if (s.part_floats < need || s.nkv < nkv) {
         cudaFree(s.part);
         cudaFree(s.counters);
+        s.part = nullptr;
+        s.counters = nullptr;
         if (cudaMalloc(&s.part, need * sizeof(float)) != cudaSuccess ||
             cudaMalloc(&s.counters, nkv * sizeof(unsigned)) != cudaSuccess ||
             (!s.rope && cudaMalloc(&s.rope, 512 * sizeof(float2)) != cudaSuccess) ||
             cudaMemset(s.counters, 0, nkv * sizeof(unsigned)) != cudaSuccess) {
+            // free whatever this attempt (or the first call) did allocate before forgetting it
+            cudaFree(s.part);
+            cudaFree(s.counters);
+            cudaFree(s.rope);
             s = AbiAttnScratch();
             xqb::set_last_error("xqk_attention_step: scratch allocation failed");
             return -4;

@@ -59,6 +59,13 @@ struct StepParams {
     int l2_ahead;        // weight chunks prefetched into L2 ahead of the ring, within a phase
     unsigned* grid_bar;  // arrival counter, 0 at launch, reset to 0 by the last arrival
     unsigned* err;
+    // Limit of every bounded wait in the launch (ns; 0 = kWaitLimitNs, 2 s).
+    unsigned long long wait_ns;
+    // Failure-detection test hook, 0 in normal launches: the grid barrier that opens phase 1
+    // waits for this many arrivals more than there are blocks. Nothing provides them, so that
+    // wait runs out after wait_ns, the kernel records kErrBarrierTimeout and every later wait
+    // returns at once; the launch ends and the host reports the error.
+    unsigned barrier_extra;
     // kPhaseEmbed
     const int* prompt;
     const uint16_t* emb;
@@ -87,6 +94,8 @@ size_t step_smem_bytes(int nslots, int slot_bytes);
 // Largest ring that fits next to the kernel's other shared memory on this device.
 int step_max_slots(int slot_bytes);
 cudaError_t step_init_device();
+// cudaFuncAttributes::binaryVersion of the loaded step kernel (100 for sm_100a), 0 on error.
+int step_kernel_binary_version();
 // Tensor map (written to `out`, kStepTmapBytes) of an fp32 vector of n floats (n a multiple of
 // 32, n / 32 a multiple of min(32, n / 32)), as the step kernel stages it.
 constexpr int kStepTmapBytes = 128;
