@@ -56,6 +56,18 @@ XQK_API int xqk_gemv_w4a16_mma(const xqk_matrix* m, const float* x_dev, float* y
  * Both tensor-core GEMVs launch with programmatic dependent launch: the weight stream may start
  * while the previous kernel in the stream finishes, x is read only after it has finished. */
 XQK_API int xqk_gemv_w4a16_mma_f16(const xqk_matrix* m, const void* x_dev, void* y_dev, void* stream);
+/* Batched W4A16 GEMM for prefill on the 5th-generation tensor cores (tcgen05.mma, fp32
+ * accumulators in tensor memory): Y[t][n] = sum_k X[t][k] W[n][k] for t < n_tokens and every
+ * row n of m. Replaces the token-serial use of gemvW4A16Neon in CustomModel::prefill
+ * (custom_model.cpp:610-640, xq_gemv_w4a16_neon.cpp:259-291) by one GEMM per matrix.
+ * x_dev: bf16 [n_tokens][cols] row-major, 16-byte aligned. x_lo_dev: NULL for one bf16 pass
+ * (W dequantised to bf16 in shared memory, then X W^T); or the bf16 residual X - X_hi for split
+ * mode, where W is also carried as a bf16 pair and three products are accumulated (relative error
+ * about 2^-16, near the fp32 path). y_dev: ldy elements per token row (ldy >= rows); out_kind 0 =
+ * store fp32, 1 = add into fp32 y, 2 = store bf16. Needs a symmetric matrix (zero 8, fp16-exact
+ * scales, group 64, kind 0 of xqk_matrix_info). Asynchronous on `stream`. */
+XQK_API int xqk_prefill_gemm_w4a16(const xqk_matrix* m, const void* x_dev, const void* x_lo_dev, int n_tokens,
+                                   void* y_dev, int ldy, int out_kind, void* stream);
 /* The tensor-core tile layout of a symmetric matrix, written to a host buffer (host only, no
  * GPU): no reference counterpart; for packaging pipelines and tests. packed: rows * cols / 2
  * bytes in the reference's nibble order, scales: rows * cols / 64 fp32 (zero 8 implied, scales

@@ -108,6 +108,12 @@ typedef struct xq_cuda_options {
     int device;        /* CUDA device ordinal; -1 = XQ_CUDA_DEVICE env var or 0 */
     int kv_fp16;       /* 1 = fp16 KV cache, 0 = fp32 KV cache (the reference's precision) */
     int use_graphs;    /* 1 = capture each decode / prefill step as a CUDA graph (default) */
+    /* 1 = prefill with every projection of a layer as one tensor-core GEMM over the prompt
+     * (tcgen05, split-bf16 operands: agrees with the token-serial prefill to about 1e-5);
+     * 0 = the reference's token-serial prefill; -1 = XQ_PREFILL_BATCHED env var or 0. Packages
+     * or contexts the batched path does not serve use the token-serial one. (Field added after
+     * use_graphs: callers built against the shorter struct get the default.) */
+    int prefill_batched;
 } xq_cuda_options;
 
 /* xq_create with an explicit device and KV precision; xq_create uses the defaults

@@ -53,8 +53,8 @@ def check_topk(s, want_v, want_i, tol=1e-4):
             assert i[k] == want_i[k], (k, i, want_i)
 
 
-def run_checkpointed(d, G, kv_fp16=False, hid_tol=1e-4, logit_tol=1e-4):
-    s = PKG.Session(d, device=0, kv_fp16=kv_fp16)
+def run_checkpointed(d, G, kv_fp16=False, hid_tol=1e-4, logit_tol=1e-4, prefill_batched=False):
+    s = PKG.Session(d, device=0, kv_fp16=kv_fp16, prefill_batched=prefill_batched)
     try:
         s.prefill(G["ids"])
         steps = list(G["steps"])
@@ -101,3 +101,21 @@ def test_cfg1_kv512_matches_reference_golden(kv_fp16):
         run_checkpointed(d, np.load(CFG1_512), kv_fp16=True, hid_tol=5e-3, logit_tol=2e-3)
     else:
         run_checkpointed(d, np.load(CFG1_512))
+
+
+@pytest.mark.skipif(not os.path.exists(P512), reason="9B 512-token golden file not generated")
+def test_9b_benchmark_shape_batched_prefill_matches_reference_golden():
+    """The same benchmark-shape golden with the prompt prefilled by the tensor-core GEMMs
+    (split-bf16 operands, sequence kernels for conv / gated delta / attention): the same bars."""
+    d = os.path.join(os.environ.get("XQ_BENCH_DIR", os.path.join(os.environ.get("TMPDIR", "/tmp"), "xq_bench")),
+                     "qwen35_9b_s2024")
+    synthetic.make_package(d, synthetic.preset("cfg2"), seed=2024)
+    run_checkpointed(d, np.load(P512), prefill_batched=True)
+
+
+@pytest.mark.skipif(not os.path.exists(CFG1_512), reason="cfg1 512-token golden file not generated")
+def test_cfg1_kv512_batched_prefill_matches_reference_golden():
+    d = os.path.join(os.environ.get("XQ_BENCH_DIR", os.path.join(os.environ.get("TMPDIR", "/tmp"), "xq_bench")),
+                     "qwen35_cfg1_s2024")
+    synthetic.make_package(d, synthetic.preset("cfg1"), seed=2024)
+    run_checkpointed(d, np.load(CFG1_512), prefill_batched=True)

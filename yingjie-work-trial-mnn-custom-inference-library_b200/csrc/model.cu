@@ -19,6 +19,8 @@
 #include <sstream>
 
 #include "model.hpp"
+#include "prefill_gemm.hpp"
+#include "prefill_ops.hpp"
 #include "mma_gemv.hpp"
 #include "ops.cuh"
 
@@ -1232,6 +1234,120 @@ bool DeviceModel::prefill(const int32_t* ids, size_t n, std::string* error) {
         return false;
     }
     return check_device_errors("prefill", error);
+}
+
+bool DeviceModel::batched_prefill_eligible(size_t n) const {
+    if (n == 0 || lm_head_.kind != 0) return false;
+    for (const DevLayer& L : layers_)
+        for (const DevMatrix* m : {&L.in_proj, &L.out_proj, &L.gate_up, &L.down})
+            if (m->kind != 0 || !m->d_rows || m->cols % 64 != 0) return false;
+    if (d_.head_dim != 256 || d_.lk_hd != 128 || d_.lv_hd % kDeltaCols != 0 || d_.conv_k != 4) return false;
+    return prefill_attn_smem(d_.heads, d_.kv_heads, d_.head_dim, static_cast<int>(n)) <= kPrefillAttnMaxSmem;
+}
+
+bool DeviceModel::prefill_batched(const int32_t* ids, size_t n, std::string* error, bool* unsupported) {
+    *unsupported = false;
+    if (!ids || n == 0) {
+        *error = "custom prefill requires prompt tokens";
+        return false;
+    }
+    if (!batched_prefill_eligible(n)) {
+        *unsupported = true;
+        *error = "batched prefill does not serve this package or context";
+        return false;
+    }
+    cudaSetDevice(opts_.device);
+    if (!reset(error)) return false;
+    if (!ensure_capacity(static_cast<int>(n), error)) return false;
+    const ModelDims& d = d_;
+    const int C = kPrefillChunk;
+    if (!pf_H_) {
+        pf_kmax_ = std::max({d.hidden, d.inter, d.lv_dim, d.heads * d.head_dim});
+        pf_ymax_ = std::max(lm_head_.cols, 0);
+        for (const DevLayer& L : layers_) pf_ymax_ = std::max({pf_ymax_, L.in_proj.rows, L.gate_up.rows});
+        if (!dev_alloc(&pf_H_, static_cast<size_t>(C) * d.hidden, error) ||
+            !dev_alloc(&pf_Y_, static_cast<size_t>(C) * pf_ymax_, error) ||
+            !dev_alloc(&pf_conv_, static_cast<size_t>(C) * d.conv_dim, error) ||
+            !dev_alloc(&pf_O_, static_cast<size_t>(C) * d.lv_dim, error) ||
+            !dev_alloc(&pf_Q_, static_cast<size_t>(C) * d.heads * d.head_dim, error) ||
+            !dev_alloc(reinterpret_cast<uint16_t**>(&pf_xhi_), static_cast<size_t>(C) * pf_kmax_, error) ||
+            !dev_alloc(reinterpret_cast<uint16_t**>(&pf_xlo_), static_cast<size_t>(C) * pf_kmax_, error) ||
+            !dev_alloc(&pf_ids_, static_cast<size_t>(C), error))
+            return false;
+    }
+    static const int passes = [] {
+        const char* v = std::getenv("XQ_PREFILL_PASSES");
+        return v && std::atoi(v) == 1 ? 1 : 3;
+    }();
+    __nv_bfloat16* xhi = static_cast<__nv_bfloat16*>(pf_xhi_);
+    __nv_bfloat16* xlo = passes == 1 ? nullptr : static_cast<__nv_bfloat16*>(pf_xlo_);
+    cudaStream_t s = stream_;
+    const bool f16 = opts_.kv_fp16;
+    auto ok = [&](cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return true;
+        *error = std::string("batched prefill: ") + what + ": " + cudaGetErrorString(e);
+        return false;
+    };
+    auto gemm = [&](const DevMatrix& m, int nc, float* y, int ldy, int kind) {
+        if (launch_prefill_gemm(m, xhi, xlo, nc, y, ldy, kind, d_err_, num_sms_, s, step_wait_ns_)) return true;
+        *error = std::string("batched prefill: ") + last_error();
+        return false;
+    };
+    for (size_t p0 = 0; p0 < n; p0 += C) {
+        const int nc = static_cast<int>(std::min<size_t>(C, n - p0));
+        if (!ok(cudaMemcpyAsync(pf_ids_, ids + p0, sizeof(int) * nc, cudaMemcpyHostToDevice, s), "prompt upload") ||
+            !ok(prefill_embed(pf_ids_, d_emb_, pf_H_, nc, d.hidden, d.vocab, s), "embedding"))
+            return false;
+        for (DevLayer& L : layers_) {
+            if (!ok(prefill_rmsnorm_split(pf_H_, L.input_norm, nc, d.hidden, d.eps, xhi, xlo, s), "input norm"))
+                return false;
+            const int ldy = L.in_proj.rows;
+            if (!gemm(L.in_proj, nc, pf_Y_, ldy, kPgOutF32)) return false;
+            if (!L.full) {
+                // in_proj rows: [qkv (conv_dim) | z (lv_dim) | a (lv_heads) | b (lv_heads)]
+                if (!ok(prefill_conv(pf_Y_, ldy, L.conv_w, L.conv_state, pf_conv_, nc, d.conv_dim, s), "conv") ||
+                    !ok(prefill_delta(pf_conv_, d.conv_dim, pf_Y_, ldy, d.conv_dim + d.lv_dim, L.a_log, L.dt_bias,
+                                      L.rec_state, pf_O_, d.lv_dim, nc, d.lk_heads, d.lv_heads, d.lk_hd, d.lv_hd, s),
+                        "gated delta") ||
+                    !ok(prefill_gated_norm(pf_O_, d.lv_dim, pf_Y_, ldy, d.conv_dim, L.lin_norm, d.lv_heads, d.lv_hd,
+                                           d.eps, nc, xhi, xlo, s),
+                        "gated norm"))
+                    return false;
+            } else {
+                if (!ok(prefill_attn_prep(pf_Y_, ldy, L.q_norm, L.k_norm, d_rope_, d.rotary_dim / 2, pf_Q_, L.k_cache,
+                                          L.v_cache, f16, static_cast<int>(p0), nc, d.heads, d.kv_heads, d.head_dim,
+                                          d.eps, s),
+                        "attention prologue") ||
+                    !ok(prefill_attn(pf_Q_, pf_Y_, ldy, L.k_cache, L.v_cache, f16, static_cast<int>(p0), nc, d.heads,
+                                     d.kv_heads, d.head_dim, xhi, xlo, s),
+                        "attention"))
+                    return false;
+            }
+            if (!gemm(L.out_proj, nc, pf_H_, d.hidden, kPgOutAddF32)) return false;  // residual add
+            if (!ok(prefill_rmsnorm_split(pf_H_, L.post_norm, nc, d.hidden, d.eps, xhi, xlo, s), "post norm") ||
+                !gemm(L.gate_up, nc, pf_Y_, L.gate_up.rows, kPgOutF32) ||
+                !ok(prefill_swiglu(pf_Y_, L.gate_up.rows, d.inter, nc, xhi, xlo, s), "swiglu") ||
+                !gemm(L.down, nc, pf_H_, d.hidden, kPgOutAddF32))
+                return false;
+        }
+        if (p0 + nc == n &&
+            !ok(cudaMemcpyAsync(d_hidden_, pf_H_ + static_cast<size_t>(nc - 1) * d.hidden, sizeof(float) * d.hidden,
+                                cudaMemcpyDeviceToDevice, s),
+                "hidden copy"))
+            return false;
+    }
+    // positions as after n token-serial steps: pos = n - 1, next_pos = n
+    const int pos[2] = {static_cast<int>(n) - 1, static_cast<int>(n)};
+    if (!ok(cudaMemcpyAsync(d_pos_, &pos[0], sizeof(int), cudaMemcpyHostToDevice, s), "positions") ||
+        !ok(cudaMemcpyAsync(d_next_pos_, &pos[1], sizeof(int), cudaMemcpyHostToDevice, s), "positions"))
+        return false;
+    const cudaError_t e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        *error = std::string("batched prefill failed: ") + cudaGetErrorString(e);
+        return false;
+    }
+    position_ = static_cast<int>(n);
+    return check_device_errors("batched prefill", error);
 }
 
 bool DeviceModel::decode_one(int32_t* token, std::string* error) {

@@ -53,11 +53,15 @@ bool pack_b200_layout(const std::string& dir, std::string* error);
 
 struct SharedWeights;
 
+// Tokens per chunk of the batched prefill (its activation buffers are sized for this).
+constexpr int kPrefillChunk = 1024;
+
 struct Options {
     int device = 0;
     bool kv_fp16 = false;
     bool use_graphs = true;
     bool persistent = true;  // one cooperative persistent kernel per step when the model allows it
+    bool prefill_batched = false;  // prefill through the tensor-core GEMMs (prefill_batched)
     int initial_capacity = 8192;
 };
 
@@ -73,6 +77,15 @@ public:
     bool reset(std::string* error);
     // CustomModel::prefill (custom_model.cpp:610-640): reset, then one forward per token.
     bool prefill(const int32_t* ids, size_t n, std::string* error);
+    // The same prefill with every projection of a layer as one tensor-core GEMM over the prompt
+    // (chunks of up to kPrefillChunk tokens): embeddings, RMSNorm, GEMMs (split-bf16 by default,
+    // XQ_PREFILL_PASSES=1 for one bf16 pass), causal conv + the gated delta rule over the sequence,
+    // q/k norm + RoPE + KV append, causal attention, SwiGLU, residual adds. Leaves the same state
+    // as prefill() (positions, hidden, conv / recurrent states, KV cache) up to rounding.
+    // false with *unsupported set when this package's layout or the context needs the
+    // token-serial path.
+    bool prefill_batched(const int32_t* ids, size_t n, std::string* error, bool* unsupported);
+    bool batched_prefill_eligible(size_t n) const;
     // CustomModel::decodeOne (custom_model.cpp:1340-1356): sample, then forward it.
     bool decode_one(int32_t* token, std::string* error);
     // Enqueue `count` decode steps without host synchronisation; tokens land in the ring.
@@ -160,6 +173,11 @@ private:
     unsigned* d_err_ = nullptr;
     int32_t* h_token_ = nullptr;  // pinned
     unsigned* h_err_ = nullptr;   // pinned
+    // batched prefill buffers (allocated on first use, sized for kPrefillChunk tokens)
+    float *pf_H_ = nullptr, *pf_Y_ = nullptr, *pf_conv_ = nullptr, *pf_O_ = nullptr, *pf_Q_ = nullptr;
+    void *pf_xhi_ = nullptr, *pf_xlo_ = nullptr;
+    int* pf_ids_ = nullptr;
+    int pf_ymax_ = 0, pf_kmax_ = 0;
     int ring_cap_ = 1 << 16;
 
     cudaStream_t stream_ = nullptr;
