@@ -43,6 +43,14 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def bf16_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
+
+
 def package_dir(preset="cfg2"):
     base = os.environ.get("XQ_BENCH_DIR", os.path.join(os.environ.get("TMPDIR", "/tmp"), "xq_bench"))
     return os.path.join(base, f"qwen35_9b_s{SEED}" if preset == "cfg2" else f"qwen35_{preset}_s{SEED}")
@@ -280,6 +288,52 @@ def config1_step(pkg, peak_gbs, kv_fp16, steps=64):
             "l2": "inputs larger than L2 (234 MB of weights streamed per step)"}
 
 
+def config3_sweep(pkg, peak_tflops, iters=5, split=False):
+    """Config 3: the prefill W4A16 GEMM on tcgen05 / TMEM (xqk_prefill_gemm_w4a16) at M = 512,
+    2048, 8192 tokens over 4096->12288, 12288->4096 and 4096->248320: bf16 activations ~ N(0, 1),
+    symmetric int4 weights (scales ~ |N(0, 0.02)| in fp16), int4 dequantised to bf16 in shared
+    memory, fp32 accumulation in tensor memory, bf16 output. TFLOP/s = 2 M N K / CUDA-event time
+    (mean of `iters` launches after one warm-up) against the measured dense bf16 peak. With
+    split=True: the split-bf16 mode (three products, the batched prefill's default)."""
+    import torch
+
+    out = []
+    for (K, N) in ((4096, 12288), (12288, 4096), (4096, 248320)):
+        rng = np.random.default_rng(K + N)
+        packed = rng.integers(0, 256, N * K // 2, dtype=np.uint8)
+        sc = (np.abs(rng.standard_normal(N * K // 64)) * 0.02).astype(np.float16).astype(np.float32)
+        m = pkg.Matrix(packed, sc, np.full(N * K // 64, 8.0, np.float32), N, K, 64)
+        del packed, sc
+        for M in (512, 2048, 8192):
+            x = torch.randn((M, K), device="cuda").to(torch.bfloat16)
+            xl = torch.zeros_like(x) if split else None
+            y = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+            st = torch.cuda.current_stream()
+
+            def call():
+                m.prefill_gemm(x.data_ptr(), xl.data_ptr() if split else None, M, y.data_ptr(), N, 2, st.cuda_stream)
+
+            call()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(iters):
+                call()
+            e1.record(st)
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / iters
+            tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+            out.append({"M": M, "K": K, "N": N, "ms": round(ms, 4), "tflops": round(tf, 1),
+                        "frac": round(tf / peak_tflops, 4)})
+            del x, xl, y
+        m.close()
+        torch.cuda.empty_cache()
+    return {"workload": "config3: W4A16 g64 prefill GEMM sweep, bf16 activations, int4 -> bf16 in shared memory",
+            "kernel": "prefill_gemm_kernel" + ("<split, 128>" if split else "<1 pass, 256>"),
+            "mode": "split-bf16 (3 products)" if split else "one bf16 pass", "unit": "TFLOP/s",
+            "peak_tflops": peak_tflops, "peak_kind": "measured bf16 (cuBLAS burst)", "points": out}
+
+
 def cpu_baseline(model_dir, steps, preset="cfg2", prompt=PROMPT_LEN):
     """The reference's own CPU path (compiled from its sources) on the same package and context,
     on a bounded sample: a `prompt`-token prefill (untimed), then `steps` greedy decode tokens
@@ -390,6 +444,7 @@ def main():
     ids = np.random.default_rng(SEED + rank).integers(0, 248320, args.prompt).astype(np.int32)
     m = sess.prefill(ids)
     prefill_tok_s = m.prefill_tokens_per_second
+    h_serial = sess.hidden()
     sess.decode_timed(args.warmup)  # untimed warm-up steps (graph capture happens here)
     torch.cuda.synchronize()
     if world > 1:
@@ -421,7 +476,17 @@ def main():
     gemvs = [gemv_roofline(pkg, peak, engine=e, rows=r) for r in (24576, 248320) for e in ("dp4a", "mma")] \
         if rank == 0 else None
     gemv = gemvs[0] if gemvs else None
+    # batched prefill through the tensor-core GEMMs: a second session on the shared weights
+    sb = pkg.Session(d, device=local, kv_fp16=args.kv_fp16, max_context_tokens=args.prompt + 64, prefill_batched=True)
+    sb.prefill(ids)  # first call allocates its buffers
+    mb = sb.prefill(ids)
+    prefill_batched = {"value": round(mb.prefill_tokens_per_second, 1), "unit": "tok/s",
+                       "prompt": args.prompt, "hidden_rel_err_vs_token_serial":
+                       float(np.abs(sb.hidden() - h_serial).max() / max(1e-30, np.abs(h_serial).max())),
+                       "path": "tcgen05 GEMMs (split-bf16) + sequence kernels; xq_prefill wall time"}
+    sb.close()
     cfg0 = config0_gemv(pkg, peak) if rank == 0 and not args.no_extra else None
+    cfg3 = config3_sweep(pkg, bf16_peak()) if rank == 0 and not args.no_extra else None
     cfg1 = config1_step(pkg, peak, args.kv_fp16) if rank == 0 and not args.no_extra else None
     step_bytes = info.get("weight_bytes", 0)
     if rank == 0:
@@ -454,7 +519,9 @@ def main():
             "roofline": dict(roof, peak_kind=peak_kind),
             "gemv_kernel": dict(gemv, peak_kind=peak_kind) if gemv else None,
             "gemv_kernels": [dict(g, peak_kind=peak_kind) for g in gemvs] if gemvs else None,
+            "prefill_batched_tok_s": prefill_batched,
             "config0_gemv": cfg0,
+            "config3_gemm": cfg3,
             "config1_step": cfg1,
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
                     "api": "xq_decode_one"},
