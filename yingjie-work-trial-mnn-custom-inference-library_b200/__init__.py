@@ -16,7 +16,8 @@ import numpy as np
 
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG_DIR, "csrc")
-LIB_PATH = os.path.join(PKG_DIR, "lib", "libxqwen35.so")
+# XQ_LIB_PATH: load another build of the library (A/B measurements of build variants).
+LIB_PATH = os.environ.get("XQ_LIB_PATH") or os.path.join(PKG_DIR, "lib", "libxqwen35.so")
 
 XQ_OK = 0
 XQ_ERR_INVALID_ARGUMENT = -1

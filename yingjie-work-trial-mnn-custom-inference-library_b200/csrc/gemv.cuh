@@ -26,7 +26,10 @@ namespace xqb {
 
 // kMetaMma: the symmetric layout's 16-row tensor-core tiles (mma_gemv.hpp), step kernel only.
 enum MetaKind : int { kMetaSym16 = 0, kMetaAff32 = 1, kMetaMma = 2 };
-enum Prologue : int { kProPlain = 0, kProRms = 1, kProGatedRms = 2 };
+// kProHeadScale (tensor-core step kernel only): x already holds o * w * silu(z) of the gated
+// head norm (written by the DeltaNet phase); each head's values are multiplied by
+// 1 / sqrt(sum(o^2) / head_dim + eps) from head_ss, the per-slice sums of o^2.
+enum Prologue : int { kProPlain = 0, kProRms = 1, kProGatedRms = 2, kProHeadScale = 3 };
 enum Epilogue : int { kEpiStore = 0, kEpiResidual = 1, kEpiSwiglu = 2, kEpiConv = 3, kEpiArgmax = 4 };
 
 constexpr int kMaxStages = 16;
@@ -53,7 +56,9 @@ struct GemvParams {
     const float* norm_w;  // kProRms: [cols]; kProGatedRms: [head_dim]
     const float* gate_z;  // kProGatedRms: [cols]
     float eps;
-    int head_dim;  // kProGatedRms
+    int head_dim;  // kProGatedRms, kProHeadScale
+    const float* head_ss;  // kProHeadScale: [cols / head_dim][head_ss_slices]
+    int head_ss_slices;
     // epilogue
     float* out;
     float* out2;           // kEpiConv: rows >= conv_channels go here

@@ -564,7 +564,8 @@ bool DeviceModel::load(const std::string& dir, const Options& opts, std::string*
         !dev_alloc(&d_ring_ctr_, 1, error) || !dev_alloc(&d_arg_val_, num_sms_, error) ||
         !dev_alloc(&d_arg_idx_, num_sms_, error) || !dev_alloc(&d_arg_counter_, 1, error) ||
         !dev_alloc(&d_attn_part_, static_cast<size_t>(d.kv_heads) * kAttnSplits * group * (d.head_dim + 2), error) ||
-        !dev_alloc(&d_attn_counters_, d.kv_heads, error) || !dev_alloc(&d_err_, 1, error))
+        !dev_alloc(&d_attn_counters_, d.kv_heads, error) || !dev_alloc(&d_err_, 1, error) ||
+        !dev_alloc(&d_head_ss_, static_cast<size_t>(d.lv_heads) * std::max(1, d.lv_hd / kDeltaCols), error))
         return false;
     if (cudaMallocHost(&h_err_, sizeof(unsigned)) != cudaSuccess) {
         *error = "pinned allocation failed";
@@ -692,6 +693,7 @@ bool DeviceModel::persistent_eligible(int capacity) const {
         static_cast<size_t>(group) * d_.head_dim + static_cast<size_t>(group) * ((capacity + kAttnSplits - 1) / kAttnSplits);
     if (attn_floats * sizeof(float) > static_cast<size_t>(kStepAttnDynBytes)) return false;
     if (d_.lk_hd != 128 || d_.lv_hd % kDeltaCols != 0) return false;
+    if (d_.kv_heads * kAttnSplits > num_sms_) return false;  // one attention item per block
     auto ok = [&](const DevMatrix& m) {
         return m.fast() && m.kind == lm_head_.kind && m.cols / 32 <= kStepConsumers &&
                m.row_stride * 4 <= kStepSlotBytes;
@@ -759,6 +761,14 @@ bool DeviceModel::build_phases(std::string* error) {
             D.kind = kPhaseDelta;
             D.d = DeltaParams{d_conv_out_, d_zab_ + d.lv_dim, L.a_log, L.dt_bias, L.rec_state, d_attn_raw_,
                               d.lk_heads, d.lv_heads, d.lk_hd, d.lv_hd};
+            // tensor-core path: the gated head norm's elementwise part and per-slice sums of
+            // squares in the DeltaNet phase; the out_proj prologue only scales each head
+            const bool fuse_norm = meta_kind_ == kMetaMma && d_head_ss_ != nullptr;
+            if (fuse_norm) {
+                D.d.z = d_zab_;
+                D.d.norm_w = L.lin_norm;
+                D.d.head_ss = d_head_ss_;
+            }
             forward.push_back(D);
             GemvParams q = {};
             q.x = d_attn_raw_;
@@ -767,7 +777,9 @@ bool DeviceModel::build_phases(std::string* error) {
             q.head_dim = d.lv_hd;
             q.eps = d.eps;
             q.out = d_hidden_;
-            forward.push_back(gemv(L.out_proj, kProGatedRms, kEpiResidual, 1, q));
+            q.head_ss = d_head_ss_;
+            q.head_ss_slices = d.lv_hd / kDeltaCols;
+            forward.push_back(gemv(L.out_proj, fuse_norm ? kProHeadScale : kProGatedRms, kEpiResidual, 1, q));
         } else {
             GemvParams p = {};
             p.x = d_hidden_;
@@ -849,7 +861,7 @@ bool DeviceModel::build_phases(std::string* error) {
         else if (D.epi == kEpiArgmax) n = "lm_head_argmax";
         else if (D.epi == kEpiConv) n = "gemv_in_proj_conv";
         else if (D.epi == kEpiSwiglu) n = "gemv_gate_up";
-        else if (D.pro == kProGatedRms) n = "gemv_out_proj";
+        else if (D.pro == kProGatedRms || D.pro == kProHeadScale) n = "gemv_out_proj";
         else if (D.epi == kEpiStore) n = "gemv_qkv";
         else if (D.g.cols == d.inter) n = "gemv_down";
         else n = "gemv_o_proj";
@@ -874,6 +886,13 @@ bool DeviceModel::build_phases(std::string* error) {
             std::vector<PhaseDesc>& list = which == 0 ? dec : pre;
             for (int ph = 0; ph < n_phases_; ++ph) {
                 PhaseDesc& D = list[ph];
+                if (D.kind == kPhaseDelta && D.d.dk <= 256) {
+                    // the phase stages each item's recurrent-state slice with this map
+                    const size_t off = ((which * static_cast<size_t>(n_phases_) + ph) * 3) * kStepTmapBytes;
+                    if (encode_state_tmap(maps.data() + off, D.d.state, D.d.nv * D.d.dk, D.d.dv, D.d.dk))
+                        D.tmap[0] = static_cast<const uint8_t*>(d_tmaps_) + off;
+                    continue;
+                }
                 if (D.kind != kPhaseGemv) continue;
                 const GemvParams& g = D.g;
                 const float* vec[3] = {g.x, nullptr, nullptr};
@@ -1691,6 +1710,8 @@ bool DeviceModel::check_device_errors(const char* what, std::string* error) {
     std::string why;
     if (v & kErrBarrierTimeout) why += "a bounded device wait ran out of time";
     if (v & kErrBadShape) why += std::string(why.empty() ? "" : "; ") + "a kernel saw an unsupported configuration";
+    if (v & kErrAttnIndex)
+        why += std::string(why.empty() ? "" : "; ") + "an attention bounds check failed (access skipped)";
     *error = std::string(what) + " failed on the device (error word " + std::to_string(v) + "): " + why;
     return false;
 }

@@ -169,6 +169,7 @@ private:
     unsigned* d_arg_counter_ = nullptr;
     float2* d_rope_ = nullptr;  // [capacity][rotary/2] (cos, sin), rebuilt when the KV cache grows
     float* d_attn_part_ = nullptr;
+    float* d_head_ss_ = nullptr;  // DeltaNet phase -> out_proj: per-slice sums of squares
     unsigned* d_attn_counters_ = nullptr;
     unsigned* d_err_ = nullptr;
     int32_t* h_token_ = nullptr;  // pinned

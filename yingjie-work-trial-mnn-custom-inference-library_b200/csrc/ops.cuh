@@ -19,6 +19,12 @@ struct DeltaParams {
     float* state;          // [nv][dk][dv]
     float* out;            // [nv*dv]
     int nk, nv, dk, dv;
+    // Optional fused part of the gated head RMSNorm (applyGatedHeadRms, custom_model.cpp:329-349)
+    // when z is set: out = o * w * silu(z) and head_ss[vh * (dv / kDeltaCols) + slice] = the sum
+    // of o^2 over the item's columns; the consumer multiplies by 1 / sqrt(mean(o^2) + eps) per head.
+    const float* z;        // [nv*dv]
+    const float* norm_w;   // [dv], no +1
+    float* head_ss;        // [nv][dv / kDeltaCols]
 };
 
 // grid (nv, dv / kDeltaCols), block dk (= 128)

@@ -46,6 +46,7 @@ inline size_t step_act_bytes(int pro, int cols, int head_dim) {
     size_t b = 4u * static_cast<size_t>(cols);
     if (pro == kProRms) b += 4u * static_cast<size_t>(cols);
     if (pro == kProGatedRms) b += 4u * (static_cast<size_t>(cols) + static_cast<size_t>(head_dim));
+    if (pro == kProHeadScale) b += 4u * 1024u;  // per-slice sums of squares (<= 1024)
     return b;
 }                 // barriers, sums, scratch (see stepper.cu)
 
@@ -100,5 +101,8 @@ int step_kernel_binary_version();
 // 32, n / 32 a multiple of min(32, n / 32)), as the step kernel stages it.
 constexpr int kStepTmapBytes = 128;
 bool encode_vector_tmap(void* out, const float* ptr, int n);
+// Tensor map of a DeltaNet recurrent state [rows][cols] fp32 read in boxes of `box_rows` rows
+// x kDeltaCols columns (one work item's state slice).
+bool encode_state_tmap(void* out, const float* ptr, int rows, int cols, int box_rows);
 
 }  // namespace xqb
