@@ -288,7 +288,7 @@ def config1_step(pkg, peak_gbs, kv_fp16, steps=64):
             "l2": "inputs larger than L2 (234 MB of weights streamed per step)"}
 
 
-def config3_sweep(pkg, peak_tflops, iters=5, split=False):
+def config3_sweep(pkg, peak_tflops, iters=5, split=False, shapes=None, m_values=(512, 2048, 8192)):
     """Config 3: the prefill W4A16 GEMM on tcgen05 / TMEM (xqk_prefill_gemm_w4a16) at M = 512,
     2048, 8192 tokens over 4096->12288, 12288->4096 and 4096->248320: bf16 activations ~ N(0, 1),
     symmetric int4 weights (scales ~ |N(0, 0.02)| in fp16), int4 dequantised to bf16 in shared
@@ -298,13 +298,13 @@ def config3_sweep(pkg, peak_tflops, iters=5, split=False):
     import torch
 
     out = []
-    for (K, N) in ((4096, 12288), (12288, 4096), (4096, 248320)):
+    for (K, N) in shapes or ((4096, 12288), (12288, 4096), (4096, 248320)):
         rng = np.random.default_rng(K + N)
         packed = rng.integers(0, 256, N * K // 2, dtype=np.uint8)
         sc = (np.abs(rng.standard_normal(N * K // 64)) * 0.02).astype(np.float16).astype(np.float32)
         m = pkg.Matrix(packed, sc, np.full(N * K // 64, 8.0, np.float32), N, K, 64)
         del packed, sc
-        for M in (512, 2048, 8192):
+        for M in m_values:
             x = torch.randn((M, K), device="cuda").to(torch.bfloat16)
             xl = torch.zeros_like(x) if split else None
             y = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
@@ -332,6 +332,38 @@ def config3_sweep(pkg, peak_tflops, iters=5, split=False):
             "kernel": "prefill_gemm_kernel" + ("<split, 128>" if split else "<1 pass, 256>"),
             "mode": "split-bf16 (3 products)" if split else "one bf16 pass", "unit": "TFLOP/s",
             "peak_tflops": peak_tflops, "peak_kind": "measured bf16 (cuBLAS burst)", "points": out}
+
+
+def config4_batched(pkg, model_dir, peak_gbs, weight_bytes, batches=(1, 8, 64), steps=64, prompt=PROMPT_LEN,
+                    kv_fp16=False):
+    """Config 4: batched decode of the 9B package, B independent sequences with their own
+    512-token random prompts (xq_batch_*: one weight pass per step for all B tokens). value =
+    B * steps / CUDA-event time of `steps` graph-launched steps (after the untimed capture step).
+    Algorithmic bytes per step: every weight once (codes + fp16 scales), plus per sequence its
+    DeltaNet recurrent and conv states read and written and its KV cache read at the mean timed
+    context and one row written."""
+    out = []
+    kv_elem = 2 if kv_fp16 else 4
+    for B in batches:
+        b = pkg.Batch(model_dir, batch=B, max_context=prompt + steps + 8, kv_fp16=kv_fp16)
+        rng = np.random.default_rng(SEED + 4000 + B)
+        for i in range(B):
+            b.prefill(i, rng.integers(0, 248320, prompt).astype(np.int32))
+        ms, toks = b.decode_timed(steps)
+        b.close()
+        ctx = prompt + 1 + steps / 2
+        per_seq = 24 * (2 * 32 * 128 * 128 * 4 + 2 * 8192 * 3 * 4) + 8 * 2 * 4 * 256 * kv_elem * (ctx + 1)
+        alg = weight_bytes + B * per_seq
+        us = ms / steps * 1000
+        out.append({"batch": B, "tok_s": round(B * steps / (ms / 1000.0), 1), "us_per_step": round(us, 1),
+                    "algorithmic_bytes_per_step": int(alg),
+                    "roofline": {"bound": "hbm", "achieved": round(alg / (us * 1e-6) / 1e9, 1), "peak": peak_gbs,
+                                 "unit": "GB/s", "frac": round(alg / (us * 1e-6) / 1e9 / peak_gbs, 4)},
+                    "tokens_head": [int(v) for v in toks[0, :4]]})
+    return {"workload": "config4: batched decode of the 9B-shaped package, B sequences with independent 512-token "
+                        "random prompts, greedy", "steps_timed": steps, "kv_dtype": "f16" if kv_fp16 else "f32",
+            "engine": "xq_batch_decode_timed: CUDA graph per step, tcgen05 split-bf16 GEMMs with M = B",
+            "points": out}
 
 
 def cpu_baseline(model_dir, steps, preset="cfg2", prompt=PROMPT_LEN):
@@ -418,11 +450,20 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt length (512 = the benchmark shape)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the config-0 GEMV and config-1 step lines")
+    ap.add_argument("--gemm-only", default=None, metavar="M,K,N",
+                    help="time only the prefill GEMM at one config-3 shape (profiling runs), print its point")
+    ap.add_argument("--gemm-split", action="store_true", help="with --gemm-only: the split-bf16 mode")
     ap.add_argument("--preset", default="cfg2", choices=["cfg2", "small"],
                     help="synthetic package: cfg2 = the benchmark's 9B shape; small = a quick functional check")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
+    if args.gemm_only:
+        M, K, N = (int(v) for v in args.gemm_only.split(","))
+        pkg = __graft_entry__.load_package()
+        r = config3_sweep(pkg, bf16_peak(), iters=args.steps, split=args.gemm_split, shapes=((K, N),), m_values=(M,))
+        print(json.dumps(r), flush=True)
+        return 0
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -487,6 +528,8 @@ def main():
     sb.close()
     cfg0 = config0_gemv(pkg, peak) if rank == 0 and not args.no_extra else None
     cfg3 = config3_sweep(pkg, bf16_peak()) if rank == 0 and not args.no_extra else None
+    cfg4 = config4_batched(pkg, d, peak, info.get("weight_bytes", 0), kv_fp16=args.kv_fp16) \
+        if rank == 0 and not args.no_extra and args.preset == "cfg2" else None
     cfg1 = config1_step(pkg, peak, args.kv_fp16) if rank == 0 and not args.no_extra else None
     step_bytes = info.get("weight_bytes", 0)
     if rank == 0:
@@ -522,6 +565,7 @@ def main():
             "prefill_batched_tok_s": prefill_batched,
             "config0_gemv": cfg0,
             "config3_gemm": cfg3,
+            "config4_batched_decode": cfg4,
             "config1_step": cfg1,
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
                     "api": "xq_decode_one"},

@@ -152,6 +152,37 @@ XQ_API xq_status xq_cuda_decode_timed(xq_session* session, size_t n, int32_t* to
  * problems. */
 XQ_API xq_status xq_pack_b200_layout(const char* model_dir, char* error_out, size_t error_capacity);
 
+/* ---- Batched decode (no reference counterpart; the reference decodes one sequence per
+ * Session, CustomModel::decodeOne, custom_model.cpp:1340-1356) --------------------------
+ * `batch` independent sequences of one package on one device, decoded together: each step
+ * makes one pass over the weights for all of them (tensor-core GEMMs with the sequences' tokens
+ * as the rows, split-bf16 operands), while every sequence keeps its own DeltaNet state, KV cache
+ * (max_context positions) and position and follows the reference's order: greedy argmax of
+ * lm_head over its final-normed hidden state (ties to the lowest index), then the forward of
+ * that token. A sequence's tokens and hidden states equal those of its own xq_session to the
+ * GEMMs' rounding (about 1e-5).
+ *   xq_batch_create:       load the package (weights shared with its sessions on the device);
+ *                          cuda_options may be NULL (device / KV precision as for xq_create).
+ *                          XQ_ERR_MODEL for packages the tensor-core GEMMs do not serve.
+ *   xq_batch_prefill:      prefill sequence `seq` (0 <= seq < batch) with its prompt; replaces
+ *                          that sequence's state. Every sequence must be prefilled before decoding.
+ *   xq_batch_decode:       one step for all sequences; tokens[b] receives sequence b's id.
+ *                          XQ_ERR_NOT_READY until every sequence is prefilled.
+ *   xq_batch_decode_timed: `steps` steps back to back, *device_ms = their CUDA-event time on the
+ *                          batch's stream; tokens (optional) receives [steps][batch] ids. If the
+ *                          step graph has not been captured yet, one extra step runs first,
+ *                          untimed (its tokens are not returned).
+ *   xq_batch_hidden_state: post-final-norm hidden state of sequence `seq`. */
+typedef struct xq_batch xq_batch;
+XQ_API xq_status xq_batch_create(const char* model_dir, const xq_cuda_options* cuda_options, int batch,
+                                 int max_context, xq_batch** out_batch);
+XQ_API void xq_batch_destroy(xq_batch* batch);
+XQ_API xq_status xq_batch_prefill(xq_batch* batch, int seq, const int32_t* token_ids, size_t n_tokens);
+XQ_API xq_status xq_batch_decode(xq_batch* batch, int32_t* tokens);
+XQ_API xq_status xq_batch_decode_timed(xq_batch* batch, size_t steps, int32_t* tokens, double* device_ms);
+XQ_API xq_status xq_batch_hidden_state(xq_batch* batch, int seq, float* out_values, size_t value_capacity,
+                                       size_t* out_size);
+
 XQ_API xq_status xq_snapshot_size(xq_session* session, size_t* bytes);
 XQ_API xq_status xq_snapshot_save(xq_session* session, void* buffer, size_t capacity, size_t* written);
 XQ_API xq_status xq_snapshot_restore(xq_session* session, const void* buffer, size_t size);

@@ -32,6 +32,8 @@ ABI_SYMBOLS = [
     "xq_get_last_metrics", "xq_get_backend_info", "xq_get_kernel_trace_json", "xq_get_debug_json",
     "xq_get_hidden_state", "xq_run_vulkan_w4a16_selftest", "xq_create_cuda", "xq_cuda_decode_timed",
     "xq_snapshot_size", "xq_snapshot_save", "xq_snapshot_restore", "xq_pack_b200_layout",
+    "xq_batch_create", "xq_batch_destroy", "xq_batch_prefill", "xq_batch_decode", "xq_batch_decode_timed",
+    "xq_batch_hidden_state",
 ]
 KERNEL_SYMBOLS = [
     "xqk_last_error", "xqk_matrix_create", "xqk_matrix_destroy", "xqk_matrix_info", "xqk_gemv_w4a16",
@@ -99,6 +101,13 @@ def lib():
     L.xq_pack_b200_layout.argtypes = [C.c_char_p, C.c_char_p, C.c_size_t]
     L.xq_snapshot_save.argtypes = [P, P, C.c_size_t, C.POINTER(C.c_size_t)]
     L.xq_snapshot_restore.argtypes = [P, P, C.c_size_t]
+    L.xq_batch_create.argtypes = [C.c_char_p, C.POINTER(XqCudaOptions), C.c_int, C.c_int, C.POINTER(P)]
+    L.xq_batch_destroy.argtypes = [P]
+    L.xq_batch_destroy.restype = None
+    L.xq_batch_prefill.argtypes = [P, C.c_int, C.POINTER(C.c_int32), C.c_size_t]
+    L.xq_batch_decode.argtypes = [P, C.POINTER(C.c_int32)]
+    L.xq_batch_decode_timed.argtypes = [P, C.c_size_t, C.POINTER(C.c_int32), C.POINTER(C.c_double)]
+    L.xq_batch_hidden_state.argtypes = [P, C.c_int, C.POINTER(C.c_float), C.c_size_t, C.POINTER(C.c_size_t)]
     L.xqk_last_error.restype = C.c_char_p
     L.xqk_matrix_create.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(P)]
     L.xqk_matrix_destroy.argtypes = [P]
@@ -312,6 +321,67 @@ class Session:
     def close(self):
         if self.h:
             self.L.xq_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Batch:
+    """Batched decode of several independent sequences (xq_batch_*): one weight pass per step."""
+
+    def __init__(self, model_dir: str, batch: int, max_context: int, device: int = 0, kv_fp16: bool = False):
+        L = lib()
+        self.L = L
+        co = XqCudaOptions()
+        co.struct_size = C.sizeof(XqCudaOptions)
+        co.device = device
+        co.kv_fp16 = 1 if kv_fp16 else 0
+        co.use_graphs = 1
+        co.prefill_batched = -1
+        self.h = C.c_void_p()
+        st = L.xq_batch_create(model_dir.encode(), C.byref(co), batch, max_context, C.byref(self.h))
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_batch_create failed: {st} {last_error()}")
+        self.batch = batch
+
+    def prefill(self, seq: int, ids) -> None:
+        ids = np.ascontiguousarray(ids, np.int32)
+        st = self.L.xq_batch_prefill(self.h, seq, ids.ctypes.data_as(C.POINTER(C.c_int32)), ids.size)
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_batch_prefill failed: {st} {last_error()}")
+
+    def decode(self) -> np.ndarray:
+        out = np.zeros(self.batch, np.int32)
+        st = self.L.xq_batch_decode(self.h, out.ctypes.data_as(C.POINTER(C.c_int32)))
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_batch_decode failed: {st} {last_error()}")
+        return out
+
+    def decode_timed(self, steps: int):
+        """steps decode steps; returns (device_ms, tokens [steps][batch])."""
+        out = np.zeros((steps, self.batch), np.int32)
+        ms = C.c_double()
+        st = self.L.xq_batch_decode_timed(self.h, steps, out.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(ms))
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_batch_decode_timed failed: {st} {last_error()}")
+        return ms.value, out
+
+    def hidden(self, seq: int) -> np.ndarray:
+        n = C.c_size_t()
+        self.L.xq_batch_hidden_state(self.h, seq, None, 0, C.byref(n))
+        out = np.zeros(n.value, np.float32)
+        st = self.L.xq_batch_hidden_state(self.h, seq, out.ctypes.data_as(C.POINTER(C.c_float)), out.size, C.byref(n))
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_batch_hidden_state failed: {st}")
+        return out
+
+    def close(self):
+        if self.h:
+            self.L.xq_batch_destroy(self.h)
             self.h = C.c_void_p()
 
     def __del__(self):

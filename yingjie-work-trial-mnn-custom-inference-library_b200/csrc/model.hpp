@@ -132,6 +132,7 @@ public:
     const DevMatrix& lm_head() const { return lm_head_; }
     float* hidden_ptr() const { return d_hidden_; }
     float* final_norm_ptr() const { return d_final_norm_; }
+    const uint16_t* embeddings() const { return d_emb_; }
     int num_sms() const { return num_sms_; }
 
     // Launch sequences (used by graph capture and by the eager path).

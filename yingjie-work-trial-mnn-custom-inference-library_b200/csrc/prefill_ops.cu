@@ -49,9 +49,15 @@ __global__ void rmsnorm_split_kernel(const float* H, const float* w, int n, floa
 // Causal conv1d + SiLU over the sequence, then the state shift (custom_model.cpp:985-1006,
 // conv_k = 4): one thread per channel walks the tokens in order. Y: [n][ldy] projections (the
 // first `channels` columns), out: [n][channels], state: [channels][3], updated in place.
-__global__ void conv_seq_kernel(const float* Y, int ldy, const float* w, float* state, float* out, int n, int channels) {
+// blockIdx.y = sequence: rows [y n, y n + n) with its own state at state + y * state_bstride
+// (batched decode: n = 1 per sequence).
+__global__ void conv_seq_kernel(const float* Y, int ldy, const float* w, float* state, float* out, int n, int channels,
+                                size_t state_bstride) {
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= channels) return;
+    Y += static_cast<size_t>(blockIdx.y) * n * ldy;
+    out += static_cast<size_t>(blockIdx.y) * n * channels;
+    state += blockIdx.y * state_bstride;
     const float4 cw = *reinterpret_cast<const float4*>(w + static_cast<size_t>(c) * 4);
     float s0 = state[3 * c], s1 = state[3 * c + 1], s2 = state[3 * c + 2];
     for (int t = 0; t < n; ++t) {
@@ -75,11 +81,16 @@ __global__ void conv_seq_kernel(const float* Y, int ldy, const float* w, float* 
 // arithmetic token after token with the state slice held in registers (thread i = key row i).
 // q | k | v of token t: conv[t] (width 2*nk*dk + nv*dv); a, b: Y[t][ab_off + vh], [.. + nv + vh].
 // The next token's inputs are loaded while the current one is processed.
+// blockIdx.z = sequence: rows [z n, z n + n), its recurrent state at state + z * state_bstride.
 __global__ void __launch_bounds__(128) delta_seq_kernel(const float* conv, int conv_ld, const float* Y, int ldy,
                                                         int ab_off, const float* a_log_p, const float* dt_bias_p,
                                                         float* state, float* out, int out_ld, int n, int nk, int nv,
-                                                        int dk, int dv) {
+                                                        int dk, int dv, size_t state_bstride) {
     __shared__ DeltaScratch sh;
+    conv += static_cast<size_t>(blockIdx.z) * n * conv_ld;
+    Y += static_cast<size_t>(blockIdx.z) * n * ldy;
+    out += static_cast<size_t>(blockIdx.z) * n * out_ld;
+    state += blockIdx.z * state_bstride;
     const int vh = blockIdx.x, j0 = blockIdx.y * kDeltaCols;
     const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
     const int factor = max(1, nv / max(1, nk));
@@ -188,14 +199,20 @@ __global__ void gated_norm_split_kernel(const float* O, int o_ld, const float* Y
 // head RMSNorm and partial RoPE of the query (into Q [n][nq][hd]); per kv head the normed and
 // rotated k and the raw v appended to the KV cache (appendKv, custom_model.cpp:673-733). One
 // warp per (t, head) of nq + nkv; norm_rope_head is the decode path's arithmetic.
+// pos_arr (batched decode): row t is sequence t at position pos_arr[t] with its KV cache at
+// kc / vc + t * kv_bstride; null: one sequence, row t at position p0 + t.
 template <typename KV>
 __global__ void attn_prep_kernel(const float* Y, int ldy, const float* q_norm, const float* k_norm, const float2* rope,
                                  int rope_stride, float* Q, KV* kc, KV* vc, int p0, int n, int nq, int nkv, int hd,
-                                 float eps) {
+                                 float eps, const int* pos_arr, size_t kv_bstride) {
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (gw >= n * (nq + nkv)) return;
     const int t = gw / (nq + nkv), h = gw % (nq + nkv);
-    const int pos = p0 + t;
+    const int pos = pos_arr ? pos_arr[t] : p0 + t;
+    if (pos_arr) {
+        kc += t * kv_bstride;
+        vc += t * kv_bstride;
+    }
     const float* y = Y + static_cast<size_t>(t) * ldy;
     const float2* rope_row = rope + static_cast<size_t>(rope_stride) * pos;
     float v[8];
@@ -231,12 +248,17 @@ __global__ void attn_prep_kernel(const float* Y, int ldy, const float* q_norm, c
 template <typename KV>
 __global__ void __launch_bounds__(256) attn_causal_kernel(const float* Q, const float* Y, int ldy, const KV* kc,
                                                           const KV* vc, int p0, int nq, int nkv, int hd,
-                                                          __nv_bfloat16* hi, __nv_bfloat16* lo) {
+                                                          __nv_bfloat16* hi, __nv_bfloat16* lo, const int* pos_arr,
+                                                          size_t kv_bstride) {
     extern __shared__ float dyn[];
     const int t = blockIdx.x, kh = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int group = nq / nkv;
-    const int L = p0 + t + 1;
+    const int L = (pos_arr ? pos_arr[t] : p0 + t) + 1;
+    if (pos_arr) {
+        kc += t * kv_bstride;
+        vc += t * kv_bstride;
+    }
     float* qs = dyn;               // [group][hd]
     float* sc = dyn + group * hd;  // [group][L]
     __shared__ float red_m[kAttnMaxGroup], red_l[kAttnMaxGroup];
@@ -310,7 +332,51 @@ __global__ void swiglu_split_kernel(const float* Y, int ldy, int inter, int n, _
     store_split(hi, lo, e, dsilu(gu.x) * gu.y);
 }
 
+// Row argmax, ties to the lowest index (gemvW4A16ArgmaxNeon, xq_gemv_w4a16_neon.cpp:315-318): one
+// block of 1024 threads per row. A NaN never wins (as with the reference's `>` comparisons).
+__global__ void __launch_bounds__(1024) row_argmax_kernel(const float* logits, int n, int* idx) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    const float* x = logits + static_cast<size_t>(blockIdx.x) * n;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int k = threadIdx.x; k < n; k += blockDim.x) {
+        const float v = x[k];
+        if (v > bv) {  // k increases: a later equal value never replaces an earlier one
+            bv = v;
+            bi = k;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = bv;
+        si[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) {
+                bv = sv[w];
+                bi = si[w];
+            }
+        idx[blockIdx.x] = (bi >= 0 && bi < n) ? bi : 0;
+    }
+}
+
 }  // namespace
+
+cudaError_t batch_argmax(const float* logits, int rows, int n, int* idx, cudaStream_t s) {
+    row_argmax_kernel<<<rows, 1024, 0, s>>>(logits, n, idx);
+    return cudaGetLastError();
+}
 
 cudaError_t prefill_embed(const int* ids, const uint16_t* emb, float* H, int n, int hidden, int vocab, cudaStream_t s) {
     embed_rows_kernel<<<n, 256, 0, s>>>(ids, emb, H, hidden, vocab);
@@ -324,17 +390,19 @@ cudaError_t prefill_rmsnorm_split(const float* H, const float* w, int n, int wid
 }
 
 cudaError_t prefill_conv(const float* Y, int ldy, const float* w, float* state, float* out, int n, int channels,
-                         cudaStream_t s) {
-    conv_seq_kernel<<<(channels + 127) / 128, 128, 0, s>>>(Y, ldy, w, state, out, n, channels);
+                         cudaStream_t s, int nseq, size_t state_bstride) {
+    conv_seq_kernel<<<dim3((channels + 127) / 128, nseq), 128, 0, s>>>(Y, ldy, w, state, out, n, channels,
+                                                                      state_bstride);
     return cudaGetLastError();
 }
 
 cudaError_t prefill_delta(const float* conv, int conv_ld, const float* Y, int ldy, int ab_off, const float* a_log,
                           const float* dt_bias, float* state, float* out, int out_ld, int n, int nk, int nv, int dk,
-                          int dv, cudaStream_t s) {
+                          int dv, cudaStream_t s, int nseq, size_t state_bstride) {
     if (dk != 128 || dv % kDeltaCols != 0) return cudaErrorInvalidValue;
-    delta_seq_kernel<<<dim3(nv, dv / kDeltaCols), 128, 0, s>>>(conv, conv_ld, Y, ldy, ab_off, a_log, dt_bias, state,
-                                                                out, out_ld, n, nk, nv, dk, dv);
+    delta_seq_kernel<<<dim3(nv, dv / kDeltaCols, nseq), 128, 0, s>>>(conv, conv_ld, Y, ldy, ab_off, a_log, dt_bias,
+                                                                      state, out, out_ld, n, nk, nv, dk, dv,
+                                                                      state_bstride);
     return cudaGetLastError();
 }
 
@@ -347,17 +415,17 @@ cudaError_t prefill_gated_norm(const float* O, int o_ld, const float* Y, int ldy
 
 cudaError_t prefill_attn_prep(const float* Y, int ldy, const float* q_norm, const float* k_norm, const float2* rope,
                               int rope_stride, float* Q, void* kc, void* vc, bool kv_fp16, int p0, int n, int nq,
-                              int nkv, int hd, float eps, cudaStream_t s) {
+                              int nkv, int hd, float eps, cudaStream_t s, const int* pos_arr, size_t kv_bstride) {
     if (hd != 256) return cudaErrorInvalidValue;
     const int warps = n * (nq + nkv);
     if (kv_fp16)
         attn_prep_kernel<__half><<<(warps + 7) / 8, 256, 0, s>>>(Y, ldy, q_norm, k_norm, rope, rope_stride, Q,
                                                                 static_cast<__half*>(kc), static_cast<__half*>(vc), p0,
-                                                                n, nq, nkv, hd, eps);
+                                                                n, nq, nkv, hd, eps, pos_arr, kv_bstride);
     else
         attn_prep_kernel<float><<<(warps + 7) / 8, 256, 0, s>>>(Y, ldy, q_norm, k_norm, rope, rope_stride, Q,
                                                                static_cast<float*>(kc), static_cast<float*>(vc), p0, n,
-                                                               nq, nkv, hd, eps);
+                                                               nq, nkv, hd, eps, pos_arr, kv_bstride);
     return cudaGetLastError();
 }
 
@@ -367,9 +435,10 @@ size_t prefill_attn_smem(int nq, int nkv, int hd, int max_len) {
 }
 
 cudaError_t prefill_attn(const float* Q, const float* Y, int ldy, const void* kc, const void* vc, bool kv_fp16, int p0,
-                         int n, int nq, int nkv, int hd, __nv_bfloat16* hi, __nv_bfloat16* lo, cudaStream_t s) {
+                         int n, int nq, int nkv, int hd, __nv_bfloat16* hi, __nv_bfloat16* lo, cudaStream_t s,
+                         const int* pos_arr, size_t kv_bstride, int max_len) {
     if (hd != 256 || nq % nkv != 0 || nq / nkv > kAttnMaxGroup) return cudaErrorInvalidValue;
-    const size_t smem = prefill_attn_smem(nq, nkv, hd, p0 + n);
+    const size_t smem = prefill_attn_smem(nq, nkv, hd, pos_arr ? max_len : p0 + n);
     if (smem > kPrefillAttnMaxSmem) return cudaErrorInvalidValue;
     cudaError_t e;
     if (kv_fp16) {
@@ -378,14 +447,14 @@ cudaError_t prefill_attn(const float* Q, const float* Y, int ldy, const void* kc
         if (e != cudaSuccess) return e;
         attn_causal_kernel<__half><<<dim3(n, nkv), 256, smem, s>>>(Q, Y, ldy, static_cast<const __half*>(kc),
                                                                    static_cast<const __half*>(vc), p0, nq, nkv, hd, hi,
-                                                                   lo);
+                                                                   lo, pos_arr, kv_bstride);
     } else {
         e = cudaFuncSetAttribute(attn_causal_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kPrefillAttnMaxSmem);
         if (e != cudaSuccess) return e;
         attn_causal_kernel<float><<<dim3(n, nkv), 256, smem, s>>>(Q, Y, ldy, static_cast<const float*>(kc),
                                                                   static_cast<const float*>(vc), p0, nq, nkv, hd, hi,
-                                                                  lo);
+                                                                  lo, pos_arr, kv_bstride);
     }
     return cudaGetLastError();
 }
