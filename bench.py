@@ -453,6 +453,8 @@ def main():
     ap.add_argument("--gemm-only", default=None, metavar="M,K,N",
                     help="time only the prefill GEMM at one config-3 shape (profiling runs), print its point")
     ap.add_argument("--gemm-split", action="store_true", help="with --gemm-only: the split-bf16 mode")
+    ap.add_argument("--batch-only", type=int, default=0, metavar="B",
+                    help="time only batched decode (config 4) at batch B, --steps steps (profiling runs)")
     ap.add_argument("--preset", default="cfg2", choices=["cfg2", "small"],
                     help="synthetic package: cfg2 = the benchmark's 9B shape; small = a quick functional check")
     args = ap.parse_args()
@@ -462,6 +464,17 @@ def main():
         M, K, N = (int(v) for v in args.gemm_only.split(","))
         pkg = __graft_entry__.load_package()
         r = config3_sweep(pkg, bf16_peak(), iters=args.steps, split=args.gemm_split, shapes=((K, N),), m_values=(M,))
+        print(json.dumps(r), flush=True)
+        return 0
+    if args.batch_only:
+        pkg = __graft_entry__.load_package()
+        d = make_package(0, 1, args.preset)
+        import torch
+
+        torch.cuda.set_device(0)
+        w = json.loads(pkg.Session(d, device=0).json("backend")).get("weight_bytes", 0)
+        peak, _ = peaks()
+        r = config4_batched(pkg, d, peak, w, batches=(args.batch_only,), steps=args.steps, kv_fp16=args.kv_fp16)
         print(json.dumps(r), flush=True)
         return 0
     rank = int(os.environ.get("RANK", "0"))

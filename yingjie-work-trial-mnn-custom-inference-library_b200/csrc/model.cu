@@ -21,6 +21,7 @@
 #include "model.hpp"
 #include "prefill_gemm.hpp"
 #include "prefill_ops.hpp"
+#include "generic.hpp"
 #include "mma_gemv.hpp"
 #include "ops.cuh"
 
@@ -99,6 +100,17 @@ void add_one(std::vector<float>* v) {
 
 std::string shape_str(const HostMatrix& m) { return std::to_string(m.rows) + "x" + std::to_string(m.cols); }
 
+// Whether an XQ4 file's group size (header field 4) is `group` (false when unreadable).
+bool package_group_is(const std::string& path, uint32_t group) {
+    std::ifstream in(path, std::ios::binary);
+    char head[28] = {};
+    in.read(head, sizeof head);
+    if (!in) return false;
+    uint32_t g = 0;
+    std::memcpy(&g, head + 20, 4);
+    return g == group;
+}
+
 bool expect_shape(const HostMatrix& m, int rows, int cols, const std::string& name, std::string* error) {
     if (m.rows != rows || m.cols != cols) {
         *error = "unexpected shape for " + name + ": " + shape_str(m) + ", expected " + std::to_string(rows) + "x" +
@@ -146,6 +158,7 @@ DeviceModel::~DeviceModel() {
         cudaFree(L.v_cache);
     }
     cudaFree(d_rope_);
+    cudaFree(d_gscore_);
     cudaFree(d_phases_decode_);
     cudaFree(d_tmaps_);
     cudaFree(d_phases_prefill_);
@@ -365,8 +378,8 @@ std::shared_ptr<WeightsEntry> weights_entry(const std::string& key) {
     return e;
 }
 
-bool load_shared_weights(const std::string& dir, const ModelDims& d, int n_layers, bool want_tiles, SharedWeights* w,
-                         std::string* error) {
+bool load_shared_weights(const std::string& dir, const ModelDims& d, int n_layers, bool want_tiles, bool generic,
+                         SharedWeights* w, std::string* error) {
     std::vector<float> v;
     if (!read_vec(dir + "/norm_weight.f32", d.hidden, &v, error)) return false;
     add_one(&v);
@@ -378,10 +391,32 @@ bool load_shared_weights(const std::string& dir, const ModelDims& d, int n_layer
     {
         std::vector<bool> full;
         const std::vector<FusedSpec> specs = fused_specs(dir, d, n_layers, &full);
-        w->packed_layout = file_exists(dir + kB200LayoutFile);
+        w->packed_layout = !generic && file_exists(dir + kB200LayoutFile);
         for (const FusedSpec& sp : specs) {
             DevMatrix shape;
             std::vector<uint8_t> host;
+            if (generic) {
+                // shapes the fused kernels do not take: each fused matrix in the layout its shape
+                // allows (the reference's own arrays for the generic GEMV kernel)
+                std::vector<HostMatrix> parts(sp.files.size());
+                std::vector<const HostMatrix*> ptrs;
+                for (size_t k = 0; k < sp.files.size(); ++k) {
+                    if (!read_xq4_file(sp.files[k], &parts[k], error) ||
+                        !expect_shape(parts[k], sp.shapes[k].first, sp.shapes[k].second, sp.labels[k], error))
+                        return false;
+                    ptrs.push_back(&parts[k]);
+                }
+                DevMatrix* dst = &w->lm_head;
+                if (sp.layer >= 0) {
+                    DevLayer& L = w->layers[static_cast<size_t>(sp.layer)];
+                    L.full = full[static_cast<size_t>(sp.layer)];
+                    dst = sp.slot == 0 ? &L.in_proj : sp.slot == 1 ? &L.out_proj : sp.slot == 2 ? &L.gate_up : &L.down;
+                }
+                if (!upload_matrix(ptrs, sp.interleave, dst, error)) return false;
+                w->weight_bytes += dst->bytes;
+                w->device_bytes += dst->bytes;
+                continue;
+            }
             if (w->packed_layout) {
                 if (!read_b200_file(dir + "/b200/" + sp.name + ".b200", &shape, &host, error)) return false;
                 int rows = 0;
@@ -436,13 +471,13 @@ bool load_shared_weights(const std::string& dir, const ModelDims& d, int n_layer
             if (!w->upload(&L.dt_bias, v, error)) return false;
         }
         for (const DevMatrix* m : {&L.in_proj, &L.out_proj, &L.gate_up, &L.down}) {
-            if (!m->fast()) {
+            if (!generic && !m->fast()) {
                 *error = "layer " + std::to_string(i) + ": matrix shape not supported by the fused kernels";
                 return false;
             }
         }
     }
-    if (!w->lm_head.fast()) {
+    if (!generic && !w->lm_head.fast()) {
         *error = "lm_head shape not supported by the fused kernels";
         return false;
     }
@@ -505,15 +540,19 @@ bool DeviceModel::load(const std::string& dir, const Options& opts, std::string*
     d_ = parse_manifest(read_small_file(dir + "/xqwen35_manifest.json"), &n_layers);
     const ModelDims& d = d_;
     // Shapes the fused kernels are written for (all Qwen3.5-9B shapes satisfy them).
-    if (d.head_dim != 256 || d.rotary_dim != 64 || d.lk_hd != 128 || d.lv_hd % 32 != 0 || d.lv_hd > 1024 ||
-        (d.lv_hd & (d.lv_hd - 1)) != 0 || d.kv_heads <= 0 || d.heads % d.kv_heads != 0 ||
-        d.heads / d.kv_heads > kAttnMaxGroup || d.lk_heads <= 0 || d.lv_heads % d.lk_heads != 0 ||
-        d.conv_k < 1 || !fast_shape(d.hidden, 64) || !fast_shape(d.inter, 64) || !fast_shape(d.lv_dim, 64) ||
-        !fast_shape(d.heads * d.head_dim, 64) || n_layers <= 0) {
-        *error = "model shape not supported by the CUDA path (needs head_dim 256, rotary 64, linear key head 128, "
-                 "widths multiple of 1024, group 64)";
+    if (n_layers <= 0 || d.hidden <= 0 || d.inter <= 0 || d.vocab <= 0 || d.heads <= 0 || d.kv_heads <= 0 ||
+        d.head_dim <= 0 || d.lk_heads <= 0 || d.lv_heads <= 0 || d.lk_hd <= 0 || d.lv_hd <= 0 || d.conv_k < 1) {
+        *error = "invalid model dimensions in the manifest";
         return false;
     }
+    // Shapes the fused kernels are written for (all Qwen3.5-9B shapes satisfy them); other
+    // shapes run the generic-shape step (generic.cu) on the GPU.
+    generic_ = d.head_dim != 256 || d.rotary_dim != 64 || d.lk_hd != 128 || d.lv_hd % 32 != 0 || d.lv_hd > 1024 ||
+               (d.lv_hd & (d.lv_hd - 1)) != 0 || d.heads % d.kv_heads != 0 || d.heads / d.kv_heads > kAttnMaxGroup ||
+               d.lv_heads % d.lk_heads != 0 || !fast_shape(d.hidden, 64) || !fast_shape(d.inter, 64) ||
+               !fast_shape(d.lv_dim, 64) || !fast_shape(d.heads * d.head_dim, 64) ||
+               !package_group_is(dir + "/lm_head_weight.xq4", 64);
+    if (generic_) opts_.kv_fp16 = false;  // the generic attention keeps an fp32 cache
     if (!file_exists(dir + "/embeddings_bf16.bin")) {
         *error = "missing embeddings_bf16.bin";
         return false;
@@ -522,12 +561,13 @@ bool DeviceModel::load(const std::string& dir, const Options& opts, std::string*
     // copy of every symmetric matrix in 16-row tiles, built from the same host rows.
     const char* em = std::getenv("XQ_STEP_MMA");
     const char* ep = std::getenv("XQ_PERSISTENT");
-    const bool want_tiles = opts.persistent && !(ep && std::atoi(ep) == 0) && !(em && std::atoi(em) == 0);
+    const bool want_tiles = !generic_ && opts.persistent && !(ep && std::atoi(ep) == 0) && !(em && std::atoi(em) == 0);
     {
         // Weights: shared with the other live sessions of this package on this device.
         char real[PATH_MAX];
         const std::string canon = realpath(dir.c_str(), real) ? std::string(real) : dir;
-        const std::string key = canon + "|" + std::to_string(opts.device) + "|" + (want_tiles ? "tiles" : "rows");
+        const std::string key = canon + "|" + std::to_string(opts.device) + "|" +
+                                (generic_ ? "generic" : want_tiles ? "tiles" : "rows");
         const std::shared_ptr<WeightsEntry> entry = weights_entry(key);
         std::lock_guard<std::mutex> lock(entry->mu);
         weights_ = entry->w.lock();
@@ -535,7 +575,7 @@ bool DeviceModel::load(const std::string& dir, const Options& opts, std::string*
         if (!weights_) {
             auto w = std::make_shared<SharedWeights>();
             w->device = opts.device;
-            if (!load_shared_weights(dir, d, n_layers, want_tiles, w.get(), error)) return false;
+            if (!load_shared_weights(dir, d, n_layers, want_tiles, generic_, w.get(), error)) return false;
             entry->w = w;
             weights_ = w;
         }
@@ -567,6 +607,13 @@ bool DeviceModel::load(const std::string& dir, const Options& opts, std::string*
         !dev_alloc(&d_attn_counters_, d.kv_heads, error) || !dev_alloc(&d_err_, 1, error) ||
         !dev_alloc(&d_head_ss_, static_cast<size_t>(d.lv_heads) * std::max(1, d.lv_hd / kDeltaCols), error))
         return false;
+    if (generic_) {
+        int ymax = d.hidden;
+        for (const DevLayer& L : layers_) ymax = std::max({ymax, L.in_proj.rows, L.gate_up.rows, L.out_proj.rows});
+        if (!dev_alloc(&d_gy_, static_cast<size_t>(ymax), error) ||
+            !dev_alloc(&d_gqbuf_, static_cast<size_t>(d.heads + d.kv_heads) * d.head_dim, error))
+            return false;
+    }
     if (cudaMallocHost(&h_err_, sizeof(unsigned)) != cudaSuccess) {
         *error = "pinned allocation failed";
         return false;
@@ -581,7 +628,7 @@ bool DeviceModel::load(const std::string& dir, const Options& opts, std::string*
         const char* e = std::getenv("XQ_PERSISTENT");
         const bool want = opts.persistent && !(e && std::atoi(e) == 0);
         meta_kind_ = lm_head_.kind;
-        persistent_ = want && persistent_eligible(capacity_) && step_init_device() == cudaSuccess;
+        persistent_ = want && !generic_ && persistent_eligible(capacity_) && step_init_device() == cudaSuccess;
         bool tiles = lm_head_.d_tiles != nullptr;
         for (const DevLayer& L : layers_)
             tiles = tiles && L.in_proj.d_tiles && L.out_proj.d_tiles && L.gate_up.d_tiles && L.down.d_tiles;
@@ -653,6 +700,15 @@ bool DeviceModel::alloc_kv(int capacity, std::string* error) {
         L.v_cache = v;
         device_bytes_ += 2 * per_pos * capacity;
     }
+    if (generic_) {  // the generic attention's score scratch [heads][capacity]
+        float* sc = nullptr;
+        if (cudaMalloc(&sc, sizeof(float) * static_cast<size_t>(d_.heads) * capacity) != cudaSuccess) {
+            *error = "attention score scratch allocation failed";
+            return false;
+        }
+        cudaFree(d_gscore_);
+        d_gscore_ = sc;
+    }
     // RoPE table for every position the cache can hold.
     std::vector<float2> rope;
     rope_table(0, capacity, d_.rotary_dim, d_.theta, &rope);
@@ -671,7 +727,7 @@ bool DeviceModel::ensure_capacity(int needed, std::string* error) {
     if (needed <= capacity_) return true;
     int cap = capacity_;
     while (cap < needed) cap *= 2;
-    if (attention_smem_bytes(d_.heads, d_.kv_heads, d_.head_dim, cap) > 200 * 1024) {
+    if (!generic_ && attention_smem_bytes(d_.heads, d_.kv_heads, d_.head_dim, cap) > 200 * 1024) {
         *error = "context length " + std::to_string(needed) + " exceeds the attention kernel's limit";
         return false;
     }
@@ -1041,7 +1097,67 @@ bool DeviceModel::enqueue_forward(cudaStream_t s) {
     return true;
 }
 
+bool DeviceModel::gemv_any(const DevMatrix& m, const float* x, float* y, cudaStream_t s) {
+    if (m.kind == 2) return launch_gemv_generic(m, x, y, s);
+    GemvParams p = {};
+    p.x = x;
+    p.out = y;
+    p.err = d_err_;
+    LaunchCtx ctx;
+    ctx.stream = s;
+    ctx.num_sms = num_sms_;
+    ctx.pdl = false;
+    return launch_gemv(m, kProPlain, kEpiStore, p, 1, ctx);
+}
+
+// One step of the generic-shape path: the reference's per-token sequence of operations
+// (custom_model.cpp:1138-1279 for a layer, 1340-1356 for decode) with plain GEMVs and the
+// generic kernels of generic.cu.
+bool DeviceModel::enqueue_generic_step(bool decode, cudaStream_t s) {
+    const ModelDims& d = d_;
+    auto ok = [](cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return true;
+        set_last_error(std::string("generic step: ") + what + ": " + cudaGetErrorString(e));
+        return false;
+    };
+    if (decode) {
+        rmsnorm_kernel<<<1, 1024, 0, s>>>(d_hidden_, d_final_norm_, d.hidden, d.eps, d_normed_);
+        if (!gemv_any(lm_head_, d_normed_, d_logits_, s) ||
+            !ok(generic_sample(d_logits_, d.vocab, d_emb_, d_hidden_, d.hidden, d_pos_, d_next_pos_, d_token_, d_ring_,
+                               d_ring_ctr_, ring_cap_, s),
+                "sample"))
+            return false;
+    } else {
+        embed_prefill_kernel<<<1, 512, 0, s>>>(d_prompt_, d_emb_, d_hidden_, d.hidden, d.vocab, d_pos_, d_next_pos_);
+        if (!ok(cudaGetLastError(), "embedding")) return false;
+    }
+    for (DevLayer& L : layers_) {
+        rmsnorm_kernel<<<1, 1024, 0, s>>>(d_hidden_, L.input_norm, d.hidden, d.eps, d_normed_);
+        if (!gemv_any(L.in_proj, d_normed_, d_gy_, s)) return false;
+        if (!L.full) {
+            GenericLinearArgs a{d_gy_, L.conv_w, L.conv_state, L.a_log, L.dt_bias, L.rec_state, L.lin_norm, d.eps,
+                                d_conv_out_, d_attn_raw_, d.lk_heads, d.lv_heads, d.lk_hd, d.lv_hd, d.conv_k};
+            if (!ok(generic_linear_attn(a, s), "linear attention") ||
+                !gemv_any(L.out_proj, d_attn_raw_, d_normed_, s))
+                return false;
+        } else {
+            GenericAttnArgs a{d_gy_,     2 * d.heads * d.head_dim, L.q_norm, L.k_norm, d_rope_, d.rotary_dim / 2,
+                              static_cast<float*>(L.k_cache), static_cast<float*>(L.v_cache), d_pos_, d_gscore_,
+                              d_gqbuf_, d_attn_out_, d.heads, d.kv_heads, d.head_dim, d.rotary_dim, d.eps};
+            if (!ok(generic_attention(a, s), "attention") || !gemv_any(L.out_proj, d_attn_out_, d_normed_, s))
+                return false;
+        }
+        if (!ok(generic_add(d_hidden_, d_normed_, d.hidden, s), "residual")) return false;
+        rmsnorm_kernel<<<1, 1024, 0, s>>>(d_hidden_, L.post_norm, d.hidden, d.eps, d_normed_);
+        if (!gemv_any(L.gate_up, d_normed_, d_gy_, s) || !ok(generic_swiglu(d_gy_, d_ffn_, d.inter, s), "swiglu") ||
+            !gemv_any(L.down, d_ffn_, d_normed_, s) || !ok(generic_add(d_hidden_, d_normed_, d.hidden, s), "residual"))
+            return false;
+    }
+    return ok(cudaGetLastError(), "launch");
+}
+
 bool DeviceModel::enqueue_decode_step(cudaStream_t s) {
+    if (generic_) return enqueue_generic_step(true, s);
     LaunchCtx ctx;
     ctx.stream = s;
     ctx.num_sms = num_sms_;
@@ -1068,6 +1184,7 @@ bool DeviceModel::enqueue_decode_step(cudaStream_t s) {
 }
 
 bool DeviceModel::enqueue_prefill_step(cudaStream_t s) {
+    if (generic_) return enqueue_generic_step(false, s);
     if (launch_ex(embed_prefill_kernel, dim3(1), dim3(512), 0, s, pdl_enabled(), static_cast<const int*>(d_prompt_),
                   static_cast<const uint16_t*>(d_emb_), d_hidden_, d_.hidden, d_.vocab, d_pos_, d_next_pos_) !=
         cudaSuccess) {
@@ -1458,15 +1575,7 @@ bool DeviceModel::hidden(std::vector<float>* out, std::string* error) {
 bool DeviceModel::logits(std::vector<float>* out, std::string* error) {
     cudaSetDevice(opts_.device);
     rmsnorm_kernel<<<1, 1024, 0, stream_>>>(d_hidden_, d_final_norm_, d_.hidden, d_.eps, d_normed_);
-    GemvParams p = {};
-    p.x = d_normed_;
-    p.out = d_logits_;
-    p.err = d_err_;
-    LaunchCtx ctx;
-    ctx.stream = stream_;
-    ctx.num_sms = num_sms_;
-    ctx.pdl = false;
-    if (!launch_gemv(lm_head_, kProPlain, kEpiStore, p, 1, ctx)) {
+    if (!gemv_any(lm_head_, d_normed_, d_logits_, stream_)) {
         *error = last_error();
         return false;
     }

@@ -139,8 +139,13 @@ public:
     bool enqueue_decode_step(cudaStream_t s);
     bool enqueue_prefill_step(cudaStream_t s);
 
+    // Whether this model runs the generic-shape step (shapes the fused kernels do not take).
+    bool generic() const { return generic_; }
+
 private:
     bool enqueue_forward(cudaStream_t s);
+    bool enqueue_generic_step(bool decode, cudaStream_t s);
+    bool gemv_any(const DevMatrix& m, const float* x, float* y, cudaStream_t s);
     bool ensure_capacity(int needed, std::string* error);
     bool alloc_kv(int capacity, std::string* error);
     bool capture_graphs(std::string* error);
@@ -171,6 +176,8 @@ private:
     float2* d_rope_ = nullptr;  // [capacity][rotary/2] (cos, sin), rebuilt when the KV cache grows
     float* d_attn_part_ = nullptr;
     float* d_head_ss_ = nullptr;  // DeltaNet phase -> out_proj: per-slice sums of squares
+    bool generic_ = false;        // generic-shape step (generic.cu)
+    float *d_gy_ = nullptr, *d_gqbuf_ = nullptr, *d_gscore_ = nullptr;  // its scratch
     unsigned* d_attn_counters_ = nullptr;
     unsigned* d_err_ = nullptr;
     int32_t* h_token_ = nullptr;  // pinned
