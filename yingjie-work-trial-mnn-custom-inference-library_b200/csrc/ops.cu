@@ -45,6 +45,51 @@ cudaError_t launch_attention(const AttnParams& p, bool kv_fp16, size_t smem, cud
                    : launch_ex(attention_kernel<float>, grid, block, smem, s, pdl, p);
 }
 
+template <typename KV>
+__global__ void __launch_bounds__(kAttnThreads) attention_batch_kernel(const AttnParams p, int qkv_stride,
+                                                                      size_t kv_bstride, __nv_bfloat16* out_hi,
+                                                                      __nv_bfloat16* out_lo) {
+    extern __shared__ float sm[];
+    __shared__ AttnScratch sh;
+    const int b = blockIdx.z;
+    const size_t ob = static_cast<size_t>(b) * p.nq * p.hd;
+    AttnParams q = p;
+    q.qkv = p.qkv + static_cast<size_t>(b) * qkv_stride;
+    q.k_cache = static_cast<KV*>(p.k_cache) + b * kv_bstride;
+    q.v_cache = static_cast<KV*>(p.v_cache) + b * kv_bstride;
+    q.pos_ptr = p.pos_ptr + b;
+    q.part = p.part + static_cast<size_t>(b) * p.nkv * kAttnSplits * (p.nq / p.nkv) * (p.hd + 2);
+    q.counters = p.counters + b * p.nkv;
+    q.out = p.out ? p.out + ob : nullptr;
+    attention_item<KV>(q, blockIdx.x, blockIdx.y, threadIdx.x, 1, sm, &sh, out_hi ? out_hi + ob : nullptr,
+                       out_lo ? out_lo + ob : nullptr);
+}
+
+cudaError_t launch_attention_batch(const AttnParams& p, bool kv_fp16, size_t smem, int batch, int qkv_stride,
+                                   size_t kv_bstride, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, cudaStream_t s) {
+    if (!p.pos_ptr || batch < 1 || !out_hi != !out_lo || (!out_hi && !p.out)) return cudaErrorInvalidValue;
+    static std::once_flag once[64];
+    static cudaError_t attr_err[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    dev &= 63;
+    std::call_once(once[dev], [&] {
+        attr_err[dev] = cudaFuncSetAttribute(attention_batch_kernel<float>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (attr_err[dev] == cudaSuccess)
+            attr_err[dev] = cudaFuncSetAttribute(attention_batch_kernel<__half>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    });
+    if (attr_err[dev] != cudaSuccess) return attr_err[dev];
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    const dim3 grid(p.nkv, kAttnSplits, batch), block(kAttnThreads);
+    if (kv_fp16)
+        attention_batch_kernel<__half><<<grid, block, smem, s>>>(p, qkv_stride, kv_bstride, out_hi, out_lo);
+    else
+        attention_batch_kernel<float><<<grid, block, smem, s>>>(p, qkv_stride, kv_bstride, out_hi, out_lo);
+    return cudaGetLastError();
+}
+
 cudaError_t attention_init_device(int max_smem_bytes) {
     cudaError_t e = cudaFuncSetAttribute(attention_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          max_smem_bytes);

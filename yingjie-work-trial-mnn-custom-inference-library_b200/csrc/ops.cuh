@@ -4,6 +4,8 @@
 
 #include <vector>
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 
 namespace xqb {
@@ -78,6 +80,13 @@ struct AttnScratch {
 
 // Launch the attention kernel (fp16 or fp32 KV cache); grid (nkv, kAttnSplits).
 cudaError_t launch_attention(const AttnParams& p, bool kv_fp16, size_t smem, cudaStream_t s, bool pdl);
+// Batched decode: grid (nkv, kAttnSplits, batch). Sequence b reads its projections at
+// p.qkv + b * qkv_stride and its position at p.pos_ptr[b], appends to and attends over its own
+// KV cache (p.k_cache / p.v_cache + b * kv_bstride elements), and uses its own scratch
+// (p.part + b * nkv * kAttnSplits * group * (hd + 2), p.counters + b * nkv) and output rows
+// (b * nq * hd into out, or into out_hi / out_lo as a bf16 pair when those are set).
+cudaError_t launch_attention_batch(const AttnParams& p, bool kv_fp16, size_t smem, int batch, int qkv_stride,
+                                   size_t kv_bstride, __nv_bfloat16* out_hi, __nv_bfloat16* out_lo, cudaStream_t s);
 cudaError_t attention_init_device(int max_smem_bytes);
 size_t attention_smem_bytes(int nq, int nkv, int hd, int capacity);
 // Host-side RoPE table with the reference's arithmetic (applyRopeVector,

@@ -169,7 +169,8 @@ __device__ __forceinline__ void norm_rope_head(float (&v)[8], const float* w, in
 // kv head to finish merges the splits and applies the sigmoid output gate.
 template <typename KV>
 __device__ __forceinline__ void attention_item(const AttnParams& p, int kh, int split, int tid, int bar_id, float* dyn,
-                               AttnScratch* sh) {
+                               AttnScratch* sh, __nv_bfloat16* out_hi = nullptr,
+                               __nv_bfloat16* out_lo = nullptr) {
     const int lane = tid & 31, warp = tid >> 5;
     const int hd = p.hd;
     const int group = p.nq / p.nkv;
@@ -323,7 +324,14 @@ __device__ __forceinline__ void attention_item(const AttnParams& p, int kh, int 
 #pragma unroll
             for (int u = 0; u < kAttnSplits; ++u) O += part[u] * sh->pm[u * group + g];
             const int qh = kh * group + g;
-            p.out[qh * hd + tid] = (O * sh->invL[g]) * dsigmoid(gate[g]);  // output gate, custom_model.cpp:944-946
+            const float val = (O * sh->invL[g]) * dsigmoid(gate[g]);  // output gate, custom_model.cpp:944-946
+            if (out_hi) {  // batched decode: the o_proj GEMM operands as a bf16 pair
+                const __nv_bfloat16 h = __float2bfloat16_rn(val);
+                out_hi[qh * hd + tid] = h;
+                out_lo[qh * hd + tid] = __float2bfloat16_rn(val - __bfloat162float(h));
+            } else {
+                p.out[qh * hd + tid] = val;
+            }
         }
         if (tid == 0) p.counters[kh] = 0u;
     }
