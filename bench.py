@@ -334,6 +334,35 @@ def config3_sweep(pkg, peak_tflops, iters=5, split=False, shapes=None, m_values=
             "peak_tflops": peak_tflops, "peak_kind": "measured bf16 (cuBLAS burst)", "points": out}
 
 
+def tp_decode(pkg, model_dir, rank, world, local, ids, steps, warmup, kv_fp16, n_layers):
+    """Tensor-parallel decode of ONE sequence over all `world` GPUs (xq_tp_*): every rank holds
+    1/world of each matrix, two NCCL all-reduces of the hidden vector per layer and one 8-byte
+    all-gather per token. Token-serial prefill of the same prompt on every rank, `warmup` steps
+    (graph capture), then `steps` timed steps; the rate is steps / max-over-ranks device time.
+    This is strong scaling of a single stream, reported beside the replica headline."""
+    import torch.distributed as dist
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")  # 16 KB all-reduces: plain peer transfers suffice
+    uid = [pkg.Tp.unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    t = pkg.Tp(model_dir, world, rank, uid[0], max_context=len(ids) + warmup + steps + 8, device=local,
+               kv_fp16=kv_fp16)
+    try:
+        t.prefill(ids)
+        t.decode(max(1, warmup))
+        dist.barrier()
+        ms, toks = t.decode(steps)
+        ms_max = max_over_ranks(ms, world)
+    finally:
+        t.close()
+    return {"tok_s": round(steps / (ms_max / 1000.0), 2), "ms_per_token": round(ms_max / steps, 4),
+            "n_gpus": world, "steps": steps, "prompt": len(ids),
+            "collectives_per_token": {"all_reduce_hidden_f32": 2 * n_layers, "all_gather_8_bytes": 1},
+            "api": "xq_tp_decode (CUDA graph per step with the NCCL calls captured)",
+            "scaling": "strong (one sequence; 1/world of the weights per GPU)",
+            "tokens_head": [int(v) for v in toks[:8]]}
+
+
 def config4_batched(pkg, model_dir, peak_gbs, weight_bytes, batches=(1, 8, 64), steps=64, prompt=PROMPT_LEN,
                     kv_fp16=False):
     """Config 4: batched decode of the 9B package, B independent sequences with their own
@@ -450,6 +479,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt length (512 = the benchmark shape)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the config-0 GEMV and config-1 step lines")
+    ap.add_argument("--no-tp", action="store_true", help="N > 1: skip the tensor-parallel single-sequence line")
     ap.add_argument("--gemm-only", default=None, metavar="M,K,N",
                     help="time only the prefill GEMM at one config-3 shape (profiling runs), print its point")
     ap.add_argument("--gemm-split", action="store_true", help="with --gemm-only: the split-bf16 mode")
@@ -520,6 +550,13 @@ def main():
     e2e_s = time.perf_counter() - t0
     e2e_value = job_rate(e2e_steps, world, max_over_ranks(e2e_s, world))
 
+    # one sequence sharded over every GPU of the job (tensor parallel), all ranks together
+    tp = None
+    if world > 1 and not args.no_tp:
+        tp_ids = np.random.default_rng(SEED).integers(0, 248320, args.prompt).astype(np.int32)
+        tp = tp_decode(pkg, d, rank, world, local, tp_ids, args.steps, args.warmup, args.kv_fp16,
+                       32 if args.preset == "cfg2" else 2)
+
     info = json.loads(sess.json("backend"))
     if os.environ.get("XQ_STEP_TRACE") and rank == 0 and info.get("step_phase_trace"):
         # per-phase device timestamps of the step kernel (slower steps: every step syncs)
@@ -580,6 +617,7 @@ def main():
             "config3_gemm": cfg3,
             "config4_batched_decode": cfg4,
             "config1_step": cfg1,
+            "tensor_parallel_decode": tp,
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4,
                     "api": "xq_decode_one"},
             "gpu_launches": kernels_per_step * args.steps,

@@ -183,6 +183,35 @@ XQ_API xq_status xq_batch_decode_timed(xq_batch* batch, size_t steps, int32_t* t
 XQ_API xq_status xq_batch_hidden_state(xq_batch* batch, int seq, float* out_values, size_t value_capacity,
                                        size_t* out_size);
 
+/* Tensor-parallel decode of ONE sequence over `world` GPUs of a node (extension; the reference
+ * decodes on one CPU). One process per GPU, each with its own xq_tp on cuda_options->device;
+ * every rank makes the same calls in the same order. Each rank holds a slice of every matrix
+ * (column slices of q/k/v, in_proj and gate/up by head and row; K slices of o_proj, out_proj
+ * and down, summed by an NCCL all-reduce; a vocabulary slice of lm_head with a cross-rank
+ * (max, lowest index) argmax). NCCL (libnccl.so.2) is loaded at run time.
+ *   xq_tp_unique_id:       an NCCL unique id (cap >= 128 bytes), made on one rank and passed
+ *                          to every rank's xq_tp_create;
+ *   xq_tp_create:          load this rank's shard; returns once every rank has joined;
+ *   xq_tp_prefill:         token-serial prefill of the prompt (same ids on every rank);
+ *   xq_tp_decode:          `steps` greedy steps (sample, then forward); tokens[i] receives the
+ *                          i-th sampled id, *device_ms this rank's CUDA-event time of the steps
+ *                          (either pointer may be NULL);
+ *   xq_tp_hidden_state:    post-final-norm hidden state (replicated on every rank);
+ *   xq_tp_plan:            this rank's shard ranges as JSON (half-open [first, last) per
+ *                          dimension), from the package manifest alone (no GPU);
+ *   xq_tp_argmax_combine:  the cross-rank rule on host arrays: the largest value wins, equal
+ *                          values go to the lowest index, NaN never wins. */
+typedef struct xq_tp xq_tp;
+XQ_API xq_status xq_tp_unique_id(unsigned char* out, size_t capacity);
+XQ_API xq_status xq_tp_create(const char* model_dir, const xq_cuda_options* cuda_options, int world, int rank,
+                              const unsigned char* unique_id, int max_context, xq_tp** out_tp);
+XQ_API void xq_tp_destroy(xq_tp* tp);
+XQ_API xq_status xq_tp_prefill(xq_tp* tp, const int32_t* token_ids, size_t n_tokens);
+XQ_API xq_status xq_tp_decode(xq_tp* tp, size_t steps, int32_t* tokens, double* device_ms);
+XQ_API xq_status xq_tp_hidden_state(xq_tp* tp, float* out_values, size_t value_capacity, size_t* out_size);
+XQ_API xq_status xq_tp_plan(const char* model_dir, int world, int rank, char* json, size_t capacity);
+XQ_API xq_status xq_tp_argmax_combine(const float* values, const int32_t* indices, int n, int32_t* out_index);
+
 XQ_API xq_status xq_snapshot_size(xq_session* session, size_t* bytes);
 XQ_API xq_status xq_snapshot_save(xq_session* session, void* buffer, size_t capacity, size_t* written);
 XQ_API xq_status xq_snapshot_restore(xq_session* session, const void* buffer, size_t size);

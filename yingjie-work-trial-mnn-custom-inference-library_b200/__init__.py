@@ -8,6 +8,7 @@ tensors); no computation happens in Python.
 from __future__ import annotations
 
 import ctypes as C
+import json
 import os
 import subprocess
 from typing import Optional
@@ -33,7 +34,8 @@ ABI_SYMBOLS = [
     "xq_get_hidden_state", "xq_run_vulkan_w4a16_selftest", "xq_create_cuda", "xq_cuda_decode_timed",
     "xq_snapshot_size", "xq_snapshot_save", "xq_snapshot_restore", "xq_pack_b200_layout",
     "xq_batch_create", "xq_batch_destroy", "xq_batch_prefill", "xq_batch_decode", "xq_batch_decode_timed",
-    "xq_batch_hidden_state",
+    "xq_batch_hidden_state", "xq_tp_unique_id", "xq_tp_create", "xq_tp_destroy", "xq_tp_prefill", "xq_tp_decode",
+    "xq_tp_hidden_state", "xq_tp_plan", "xq_tp_argmax_combine",
 ]
 KERNEL_SYMBOLS = [
     "xqk_last_error", "xqk_matrix_create", "xqk_matrix_destroy", "xqk_matrix_info", "xqk_gemv_w4a16",
@@ -108,6 +110,15 @@ def lib():
     L.xq_batch_decode.argtypes = [P, C.POINTER(C.c_int32)]
     L.xq_batch_decode_timed.argtypes = [P, C.c_size_t, C.POINTER(C.c_int32), C.POINTER(C.c_double)]
     L.xq_batch_hidden_state.argtypes = [P, C.c_int, C.POINTER(C.c_float), C.c_size_t, C.POINTER(C.c_size_t)]
+    L.xq_tp_unique_id.argtypes = [P, C.c_size_t]
+    L.xq_tp_create.argtypes = [C.c_char_p, C.POINTER(XqCudaOptions), C.c_int, C.c_int, P, C.c_int, C.POINTER(P)]
+    L.xq_tp_destroy.argtypes = [P]
+    L.xq_tp_destroy.restype = None
+    L.xq_tp_prefill.argtypes = [P, C.POINTER(C.c_int32), C.c_size_t]
+    L.xq_tp_decode.argtypes = [P, C.c_size_t, C.POINTER(C.c_int32), C.POINTER(C.c_double)]
+    L.xq_tp_hidden_state.argtypes = [P, C.POINTER(C.c_float), C.c_size_t, C.POINTER(C.c_size_t)]
+    L.xq_tp_plan.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_char_p, C.c_size_t]
+    L.xq_tp_argmax_combine.argtypes = [C.POINTER(C.c_float), C.POINTER(C.c_int32), C.c_int, C.POINTER(C.c_int32)]
     L.xqk_last_error.restype = C.c_char_p
     L.xqk_matrix_create.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(P)]
     L.xqk_matrix_destroy.argtypes = [P]
@@ -321,6 +332,91 @@ class Session:
     def close(self):
         if self.h:
             self.L.xq_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def tp_plan(model_dir: str, world: int, rank: int) -> dict:
+    """This rank's tensor-parallel shard ranges (xq_tp_plan), half-open [first, last)."""
+    buf = C.create_string_buffer(1024)
+    st = lib().xq_tp_plan(model_dir.encode(), world, rank, buf, len(buf))
+    if st != XQ_OK:
+        raise ValueError(f"xq_tp_plan failed: {st} {last_error()}")
+    return json.loads(buf.value.decode())
+
+
+def tp_argmax_combine(values, indices) -> int:
+    """The cross-rank argmax rule (xq_tp_argmax_combine) on host arrays."""
+    v = np.ascontiguousarray(values, np.float32)
+    i = np.ascontiguousarray(indices, np.int32)
+    out = C.c_int32()
+    st = lib().xq_tp_argmax_combine(v.ctypes.data_as(C.POINTER(C.c_float)), i.ctypes.data_as(C.POINTER(C.c_int32)),
+                                    v.size, C.byref(out))
+    if st != XQ_OK:
+        raise ValueError(f"xq_tp_argmax_combine failed: {st}")
+    return out.value
+
+
+class Tp:
+    """Tensor-parallel decode of one sequence over several GPUs (xq_tp_*): one instance per
+    rank process, every rank making the same calls. `uid` is Tp.unique_id() from one rank."""
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = (C.c_ubyte * 128)()
+        st = lib().xq_tp_unique_id(buf, 128)
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_tp_unique_id failed: {st} {last_error()}")
+        return bytes(buf)
+
+    def __init__(self, model_dir: str, world: int, rank: int, uid: bytes, max_context: int, device: int = 0,
+                 kv_fp16: bool = False):
+        L = lib()
+        self.L = L
+        co = XqCudaOptions()
+        co.struct_size = C.sizeof(XqCudaOptions)
+        co.device = device
+        co.kv_fp16 = 1 if kv_fp16 else 0
+        co.use_graphs = 1
+        co.prefill_batched = -1
+        idbuf = (C.c_ubyte * 128).from_buffer_copy(uid[:128])
+        self.h = C.c_void_p()
+        st = L.xq_tp_create(model_dir.encode(), C.byref(co), world, rank, idbuf, max_context, C.byref(self.h))
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_tp_create failed: {st} {last_error()}")
+
+    def prefill(self, ids) -> None:
+        ids = np.ascontiguousarray(ids, np.int32)
+        st = self.L.xq_tp_prefill(self.h, ids.ctypes.data_as(C.POINTER(C.c_int32)), ids.size)
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_tp_prefill failed: {st} {last_error()}")
+
+    def decode(self, steps: int):
+        """steps greedy decode steps; returns (this rank's device ms, tokens)."""
+        out = np.zeros(steps, np.int32)
+        ms = C.c_double()
+        st = self.L.xq_tp_decode(self.h, steps, out.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(ms))
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_tp_decode failed: {st} {last_error()}")
+        return ms.value, out
+
+    def hidden(self) -> np.ndarray:
+        n = C.c_size_t()
+        self.L.xq_tp_hidden_state(self.h, None, 0, C.byref(n))
+        out = np.zeros(n.value, np.float32)
+        st = self.L.xq_tp_hidden_state(self.h, out.ctypes.data_as(C.POINTER(C.c_float)), out.size, C.byref(n))
+        if st != XQ_OK:
+            raise RuntimeError(f"xq_tp_hidden_state failed: {st} {last_error()}")
+        return out
+
+    def close(self):
+        if self.h:
+            self.L.xq_tp_destroy(self.h)
             self.h = C.c_void_p()
 
     def __del__(self):

@@ -146,7 +146,7 @@ bool upload_matrix(const std::vector<const HostMatrix*>& parts, bool interleave_
 }
 
 bool build_matrix_rows(const std::vector<const HostMatrix*>& parts, bool interleave_pairs, DevMatrix* out,
-                       std::vector<uint8_t>* host_out, std::string* error) {
+                       std::vector<uint8_t>* host_out, std::string* error, bool narrow) {
     const int cols = parts[0]->cols, group = parts[0]->group;
     int rows = 0;
     for (const HostMatrix* p : parts) {
@@ -156,7 +156,7 @@ bool build_matrix_rows(const std::vector<const HostMatrix*>& parts, bool interle
         }
         rows += p->rows;
     }
-    if (!fast_shape(cols, group)) {
+    if (!fast_shape(cols, group) && !(narrow && group == 64 && cols >= 512 && cols % 512 == 0)) {
         *error = "matrix shape has no fused row layout";
         return false;
     }
@@ -178,7 +178,7 @@ bool build_matrix_rows(const std::vector<const HostMatrix*>& parts, bool interle
     }
     out->kind = sym ? 0 : 1;
     out->meta_offset = cols / 2;
-    out->row_stride = cols / 2 + (sym ? 2 : 8) * gpr;  // multiple of 16 since cols % 1024 == 0
+    out->row_stride = cols / 2 + (sym ? 2 : 8) * gpr;  // multiple of 16 since cols % 512 == 0
     std::vector<uint8_t>& host = *host_out;
     host.assign(static_cast<size_t>(rows) * out->row_stride, 0);
     size_t dst_row = 0;

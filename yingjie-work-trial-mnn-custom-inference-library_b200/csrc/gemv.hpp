@@ -41,9 +41,11 @@ struct DevMatrix {
 bool fast_shape(int cols, int group);
 
 // The fused-kernel row layout of the row-wise concatenation of `parts` (as upload_matrix
-// builds it) in host memory; false (error set) when the shape has no fused layout.
+// builds it) in host memory; false (error set) when the shape has no fused layout. narrow:
+// also widths that are a multiple of 512 only (K slices of tensor-parallel shards; served by
+// the tensor-core GEMM alone, not by the GEMV kernels).
 bool build_matrix_rows(const std::vector<const HostMatrix*>& parts, bool interleave_pairs, DevMatrix* shape,
-                       std::vector<uint8_t>* host, std::string* error);
+                       std::vector<uint8_t>* host, std::string* error, bool narrow = false);
 // Device copy of rows built by build_matrix_rows (fills d_rows and bytes).
 bool upload_matrix_rows(const std::vector<uint8_t>& host, DevMatrix* m, std::string* error);
 // The packed B200 layout on disk: a 64-byte header (magic "XQB200\0\0", version, kind, rows,

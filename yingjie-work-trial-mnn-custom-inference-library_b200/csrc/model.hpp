@@ -26,6 +26,14 @@ struct ModelDims {
 // Manifest parsing with the reference's substring rules (custom_model.cpp:38-87, 431-453).
 ModelDims parse_manifest(const std::string& json, int* n_layers);
 
+// Package file helpers shared by the loaders.
+std::string read_small_file(const std::string& path);
+bool file_exists(const std::string& path);
+// `expected` floats from a raw little-endian f32 file (false, error set, when missing or short).
+bool read_vec(const std::string& path, int expected, std::vector<float>* out, std::string* error);
+// The reference's +1 on RMSNorm weights (custom_model.cpp:524).
+void add_one(std::vector<float>* v);
+
 struct DevLayer {
     bool full = false;
     DevMatrix in_proj;   // linear: [qkv | z | a | b]; full: [q(+gate) | k | v]
