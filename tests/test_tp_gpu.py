@@ -71,3 +71,28 @@ def test_tp2_cfg1_matches_reference_golden():
     for j in range(len(steps)):
         assert rel_err(h0[j], G["hidden"][j]) <= 1e-4, steps[j]
     assert t0 == list(G["tokens"])
+
+
+@pytest.mark.skipif(not os.path.exists(CFG1_512), reason="cfg1 512-token golden file not generated")
+def test_tp1_cfg1_matches_reference_golden():
+    """The tensor-parallel engine on one GPU (a one-rank NCCL communicator, whole matrices):
+    the same golden bars, on the path the multi-GPU runs take."""
+    G = np.load(CFG1_512)
+    d = os.path.join(os.environ.get("XQ_BENCH_DIR", os.path.join(os.environ.get("TMPDIR", "/tmp"), "xq_bench")),
+                     "qwen35_cfg1_s2024")
+    synthetic.make_package(d, synthetic.preset("cfg1"), seed=2024)
+    steps = [int(s) for s in G["steps"]]
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    t = PKG.Tp(d, 1, 0, PKG.Tp.unique_id(), max_context=600, device=0)
+    try:
+        t.prefill(G["ids"])
+        assert rel_err(t.hidden(), G["hidden"][0]) <= 1e-4
+        toks, done = [], 0
+        for j, k in enumerate(steps[1:], start=1):
+            _, tk = t.decode(k - done)
+            toks += list(tk)
+            done = k
+            assert rel_err(t.hidden(), G["hidden"][j]) <= 1e-4, k
+        assert toks == list(G["tokens"])
+    finally:
+        t.close()

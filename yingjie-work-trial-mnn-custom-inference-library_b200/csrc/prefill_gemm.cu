@@ -10,8 +10,8 @@
 //   warp 0      TMA producer: per 64-column K block, the X tile (128-byte swizzle, the UMMA
 //               canonical K-major layout) and the raw int4 codes + fp16 scales of 128 rows
 //               (plain 2-D tensor copies of the row layout);
-//   warp 1      allocates tensor memory; lane 0 issues tcgen05.mma (M = 128, N = NT, K = 16,
-//               four per K block) and tcgen05.commit to the mbarriers;
+//   warp 1      allocates tensor memory; one elected lane issues tcgen05.mma (M = 128, N = NT,
+//               K = 16, four per K block) and tcgen05.commit to the mbarriers;
 //   warps 2-5   dequantise: thread r turns row r's 64 codes into (code - 8) * scale, rounded to
 //               bf16 (split mode: also the bf16 residual), written into the A tile in the same
 //               swizzled K-major layout, then a generic -> async proxy fence;
@@ -464,11 +464,12 @@ __global__ void __launch_bounds__(kPgThreads, 1) prefill_gemm_kernel(const __gri
 //     [r steps / S, (r + 1) steps / S) of the cluster's row tiles; the partial tiles meet in
 //     distributed shared memory and CTA r sums rows [r 128 / S, (r + 1) 128 / S) over the S
 //     partials in rank order (deterministic; no global workspace, no atomics).
-// Roles (18 warps): warp 0 TMA (X tiles + raw codes), warp 1 TMEM + MMA issue, warps 2-9 code
-// conversion (warp w: TMEM lanes = rows 32 (w % 4) .., K block (w - 2) / 4 of the step), warps
-// 10-17 accumulation (warp w: TMEM lanes 32 (w % 4) .., token half (w - 10) / 4) and the tile's
-// output.
-constexpr int kDgThreads = 576;
+// Roles (19 warps): warp 0 TMA (X tiles + raw codes), warps 1 and 18 MMA issue (even and odd
+// steps: one warp's barrier waits and commits overlap the other's MMAs; warp 1 also owns the
+// tensor memory), warps 2-9 code conversion (warp w: TMEM lanes = rows 32 (w % 4) .., K block
+// (w - 2) / 4 of the step), warps 10-17 accumulation (warp w: TMEM lanes 32 (w % 4) .., token
+// half (w - 10) / 4) and the tile's output.
+constexpr int kDgThreads = 608;  // 19 warps
 constexpr int kDgConvWarps = 8;
 constexpr int kDgAccWarps = 8;
 constexpr int kDgKb = 2;           // K blocks per pipeline step
@@ -597,14 +598,22 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
     producer_done:
         for (uint32_t k = g > LS ? g - LS : 0; k < g; ++k) mbar_wait_drain(&load_full[k % LS], (k / LS) & 1);
         __syncwarp();
-    } else if (warp == 1) {
-        // ---------------- MMA issuer (whole warp, one elected lane issues) ----------------
-        // (a_full implies load_full: the converters waited for the stage before converting it)
+    } else if (warp == 1 || warp == 2 + kDgConvWarps + kDgAccWarps) {
+        // ---------------- MMA issuers (whole warp, one elected lane issues) ----------------
+        // warp 1 issues the even steps, the last warp the odd ones; each commits (and so tracks)
+        // only its own MMAs. a_full implies load_full: the converters waited for the stage.
+        // With a single accumulator buffer one issuer could wait on acc_empty a full phase
+        // ahead of the other, where a parity wait cannot tell the phases apart: warp 1 then
+        // issues every step alone.
+        constexpr bool kTwoIssuers = RB >= 2;
+        const bool return_role = !kTwoIssuers && warp != 1;
+        const uint32_t parity = warp == 1 ? 0u : 1u;
         const uint32_t idesc = f16_idesc(kPgRows, split ? 2 * NT : NT);
-        uint32_t g = 0;
-        bool ok = true;
+        uint32_t g = 0, last = 0;
+        bool ok = true, any = false;
         for (int tile = cid; tile < tiles && ok; tile += ncl) {
             for (int st = st0; st < st1; ++st, ++g) {
+                if (return_role || (kTwoIssuers && (g & 1u) != parity)) continue;
                 const int s = g % LS, as = g % AS, b = g % RB;
                 ok = warp_wait(&a_full[as], (g / AS) & 1, p.err, wait_ns) &&
                      (g < static_cast<uint32_t>(RB) || warp_wait(&acc_empty[b], ((g / RB) - 1) & 1, p.err, wait_ns));
@@ -623,9 +632,11 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
                 tc_commit_elect(&load_empty[s]);
                 tc_commit_elect(&a_empty[as]);
                 tc_commit_elect(&acc_full[b]);
+                last = g;
+                any = true;
             }
         }
-        if (g > 0) mbar_wait_drain(&acc_full[(g - 1) % RB], ((g - 1) / RB) & 1);
+        if (any) mbar_wait_drain(&acc_full[last % RB], (last / RB) & 1);
         __syncwarp();
     } else if (warp < 2 + kDgConvWarps) {
         // ---------------- code conversion (into the TMEM A stage) ----------------
@@ -899,7 +910,16 @@ bool launch_prefill_gemm(const DevMatrix& w, const __nv_bfloat16* x, const __nv_
     const int K = w.cols;
     const bool split = x_lo != nullptr;
     static const bool small_m_kernel = env_int("XQ_GEMM_SMALL_M", 1) != 0;
-    const int small_nt = (!small_m_kernel || K % (kPgKb * kDgKb) != 0) ? 0 : M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 0;
+    // widest token tile of the small-M kernel (16, 32 or 64); a narrower one covers M in several
+    // token tiles whose CTAs share each weight tile through L2
+    // (32 by default: at M = 64 two 32-token tiles with two accumulators in flight measured up to
+    // 1.3x faster per layer matrix than one 64-token tile, which has room for one)
+    static const int small_nt_max = env_int("XQ_GEMM_SMALL_NT_MAX", 32);
+    const int small_nt = (!small_m_kernel || K % (kPgKb * kDgKb) != 0) ? 0
+                         : M <= 16                                     ? 16
+                         : M <= 32 || (small_nt_max < 64 && M <= 64)   ? std::min(32, std::max(16, small_nt_max))
+                         : M <= 64                                     ? 64
+                                                                       : 0;
     const int NT = small_nt ? small_nt : split ? 128 : 256;
     bool ok = encode_2d(&p.map_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, K, M, 2ull * K, kPgKb, NT,
                         CU_TENSOR_MAP_SWIZZLE_128B) &&
