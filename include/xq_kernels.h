@@ -65,7 +65,11 @@ XQK_API int xqk_gemv_w4a16_mma_f16(const xqk_matrix* m, const void* x_dev, void*
  * mode, where W is also carried as a bf16 pair and three products are accumulated (relative error
  * about 2^-16, near the fp32 path). y_dev: ldy elements per token row (ldy >= rows); out_kind 0 =
  * store fp32, 1 = add into fp32 y, 2 = store bf16. Needs a symmetric matrix (zero 8, fp16-exact
- * scales, group 64, kind 0 of xqk_matrix_info). Asynchronous on `stream`. */
+ * scales, group 64, kind 0 of xqk_matrix_info). Asynchronous on `stream`.
+ * n_tokens <= 64 (batched decode, short prompt chunks) runs a small-M kernel that multiplies the
+ * exact integer codes and applies each group's scale to that group's fp32 partial sum: W is then
+ * exact in both modes (one pass: bf16 X times the exact W), and its split-K reduction across a
+ * thread-block cluster has a fixed order, so results are bit-reproducible run to run. */
 XQK_API int xqk_prefill_gemm_w4a16(const xqk_matrix* m, const void* x_dev, const void* x_lo_dev, int n_tokens,
                                    void* y_dev, int ldy, int out_kind, void* stream);
 /* The tensor-core tile layout of a symmetric matrix, written to a host buffer (host only, no

@@ -96,3 +96,48 @@ def test_tp1_cfg1_matches_reference_golden():
         assert toks == list(G["tokens"])
     finally:
         t.close()
+
+
+def test_tp2_shared_kv_head_matches_single_gpu_session():
+    """More ranks than kv heads (the N = 8 layout of the 9B model, here on two GPUs): one kv
+    head, replicated on both ranks, each rank with half of the query heads. Tokens and hidden
+    states equal the single-GPU session's (itself pinned to the reference)."""
+    if _gpus() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    cfg = synthetic.ModelConfig(hidden_size=2048, intermediate_size=2048, vocab_size=4096, num_attention_heads=8,
+                                num_key_value_heads=1, head_dim=256, linear_num_key_heads=8, linear_num_value_heads=16,
+                                layer_types=["linear_attention", "full_attention"])
+    d = os.path.join(os.environ.get("XQ_BENCH_DIR", os.path.join(os.environ.get("TMPDIR", "/tmp"), "xq_bench")),
+                     "tp_shared_kv_s5")
+    synthetic.make_package(d, cfg, seed=5)
+    assert PKG.tp_plan(d, 2, 0)["kv_heads"] == PKG.tp_plan(d, 2, 1)["kv_heads"] == [0, 1]
+    ids = np.random.default_rng(8).integers(0, 4096, 40).astype(np.int32)
+    steps = [0, 1, 6]
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    uid = PKG.Tp.unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, 2, uid, d, ids, steps, q), daemon=True) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = sorted(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for rank, status, _, _ in got:
+        assert status == "ok", (rank, status)
+    (_, _, t0, h0), (_, _, t1, h1) = got
+    assert np.array_equal(h0, h1) and t0 == t1
+    s = PKG.Session(d, device=0)
+    try:
+        s.prefill(ids)
+        assert rel_err(h0[0], s.hidden()) <= 1e-4
+        toks = []
+        for j, k in enumerate(steps[1:], start=1):
+            while len(toks) < k:
+                toks.append(s.decode_one())
+            assert rel_err(h0[j], s.hidden()) <= 1e-4, k
+        assert t0 == toks
+    finally:
+        s.close()
