@@ -323,13 +323,17 @@ def config3_sweep(pkg, peak_tflops, iters=5, split=False, shapes=None, m_values=
             torch.cuda.synchronize()
             ms = e0.elapsed_time(e1) / iters
             tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
-            out.append({"M": M, "K": K, "N": N, "ms": round(ms, 4), "tflops": round(tf, 1),
-                        "frac": round(tf / peak_tflops, 4)})
+            pt = {"M": M, "K": K, "N": N, "ms": round(ms, 4), "tflops": round(tf, 1),
+                  "frac": round(tf / peak_tflops, 4)}
+            if M <= 64:  # the small-M kernel (exact codes in tensor memory): weight-stream bound
+                pt["kernel"] = "decode_gemm_kernel"
+                pt["weights_gb_s"] = round(N * K * 0.53125 / (ms * 1e-3) / 1e9, 1)
+            out.append(pt)
             del x, xl, y
         m.close()
         torch.cuda.empty_cache()
     return {"workload": "config3: W4A16 g64 prefill GEMM sweep, bf16 activations, int4 -> bf16 in shared memory",
-            "kernel": "prefill_gemm_kernel" + ("<split, 128>" if split else "<1 pass, 256>"),
+            "kernel": "prefill_gemm_kernel" + ("<split, 128>" if split else "<1 pass, 256>") + " (M > 64)",
             "mode": "split-bf16 (3 products)" if split else "one bf16 pass", "unit": "TFLOP/s",
             "peak_tflops": peak_tflops, "peak_kind": "measured bf16 (cuBLAS burst)", "points": out}
 
