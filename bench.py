@@ -484,6 +484,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the config-0 GEMV and config-1 step lines")
     ap.add_argument("--no-tp", action="store_true", help="N > 1: skip the tensor-parallel single-sequence line")
+    ap.add_argument("--cpu-prompt", type=int, default=32,
+                    help="prompt tokens before the cpu_baseline's timed decode steps (its prefill runs at the "
+                         "reference's ~2.5 tok/s; the reference arm keeps --prompt)")
     ap.add_argument("--gemm-only", default=None, metavar="M,K,N",
                     help="time only the prefill GEMM at one config-3 shape (profiling runs), print its point")
     ap.add_argument("--gemm-split", action="store_true", help="with --gemm-only: the split-bf16 mode")
@@ -580,11 +583,13 @@ def main():
                        float(np.abs(sb.hidden() - h_serial).max() / max(1e-30, np.abs(h_serial).max())),
                        "path": "tcgen05 GEMMs (split-bf16) + sequence kernels; xq_prefill wall time"}
     sb.close()
-    cfg0 = config0_gemv(pkg, peak) if rank == 0 and not args.no_extra else None
-    cfg3 = config3_sweep(pkg, bf16_peak()) if rank == 0 and not args.no_extra else None
+    # the per-config lines run at N = 1 (at N > 1 the job measures replicas and tensor parallel)
+    extra = world == 1 and not args.no_extra
+    cfg0 = config0_gemv(pkg, peak) if extra else None
+    cfg3 = config3_sweep(pkg, bf16_peak()) if extra else None
     cfg4 = config4_batched(pkg, d, peak, info.get("weight_bytes", 0), kv_fp16=args.kv_fp16) \
-        if rank == 0 and not args.no_extra and args.preset == "cfg2" else None
-    cfg1 = config1_step(pkg, peak, args.kv_fp16) if rank == 0 and not args.no_extra else None
+        if extra and args.preset == "cfg2" else None
+    cfg1 = config1_step(pkg, peak, args.kv_fp16) if extra else None
     step_bytes = info.get("weight_bytes", 0)
     if rank == 0:
         # Algorithmic bytes of one decode step: every weight matrix once (codes + fp16 scales),
@@ -629,7 +634,7 @@ def main():
             "tokens_head": [int(v) for v in toks[:8]],
         }
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(d, args.cpu_steps, args.preset, prompt=args.prompt)
+            line["cpu_baseline"] = cpu_baseline(d, args.cpu_steps, args.preset, prompt=args.cpu_prompt)
         if args.preset != "cfg2":
             line["config"]["workload"] = f"{args.preset} preset (functional check, not a bench line)"
         print(json.dumps(line), flush=True)
