@@ -457,34 +457,36 @@ __global__ void __launch_bounds__(kPgThreads, 1) prefill_gemm_kernel(const __gri
 //     acc += scale(row, group) * (W X_hi + W X_lo), so W is exact and the error is X's split;
 //   * X_hi and X_lo sit in one B tile of 2 NT rows: one MMA (M = 128, N = 2 NT, K = 16) per
 //     16 columns computes both products;
-//   * the pipeline moves two K blocks per step (one wait and one commit per barrier per step):
-//     every barrier operation costs the issuing warp about as much as one MMA, so per-step
-//     signalling is amortised over eight MMAs;
+//   * the pipeline moves several K blocks per step (four at NT = 16, else two; one wait and one
+//     commit per barrier per step): the barrier operations of a step cost the issuing warp about
+//     as much as eight MMAs, so they are amortised over 16 (or 8) MMAs;
 //   * split-K over a thread-block cluster of S CTAs: CTA r of the cluster takes steps
 //     [r steps / S, (r + 1) steps / S) of the cluster's row tiles; the partial tiles meet in
 //     distributed shared memory and CTA r sums rows [r 128 / S, (r + 1) 128 / S) over the S
 //     partials in rank order (deterministic; no global workspace, no atomics).
 // Roles (19 warps): warp 0 TMA (X tiles + raw codes), warps 1 and 18 MMA issue (even and odd
 // steps: one warp's barrier waits and commits overlap the other's MMAs; warp 1 also owns the
-// tensor memory), warps 2-9 code conversion (warp w: TMEM lanes = rows 32 (w % 4) .., K block
-// (w - 2) / 4 of the step), warps 10-17 accumulation (warp w: TMEM lanes 32 (w % 4) .., token
+// tensor memory), warps 2-9 code conversion (warp w: TMEM lanes = rows 32 (w % 4) .., K blocks
+// (w - 2) / 4, + 2, .. of the step), warps 10-17 accumulation (warp w: TMEM lanes 32 (w % 4) .., token
 // half (w - 10) / 4) and the tile's output.
 constexpr int kDgThreads = 608;  // 19 warps
 constexpr int kDgConvWarps = 8;
 constexpr int kDgAccWarps = 8;
-constexpr int kDgKb = 2;           // K blocks per pipeline step
 constexpr int kDgTmemCols = 512;   // the whole tensor memory: accumulators + A stages
-constexpr int kDgACols = kDgKb * 32;  // one A stage in TMEM: 128 lanes x 2 K blocks of bf16 pairs
 
 template <int NT>
 struct DgCfg {
-    static constexpr int kAccBufs = NT == 64 ? 1 : (NT == 32 ? 2 : 4);  // steps in flight in TMEM
-    static constexpr int kAccCols = kAccBufs * kDgKb * 2 * NT;
-    static constexpr int kAStages = (kDgTmemCols - kAccCols) / kDgACols;
-    static constexpr int kLoadStages = NT == 64 ? 4 : (NT == 32 ? 6 : 8);
+    // K blocks per pipeline step: four at NT = 16 (the barrier waits and commits of a step,
+    // ~500 cycles, spread over 16 MMAs), two where four would not leave two steps in TMEM
+    static constexpr int kKb = NT == 16 ? 4 : 2;
+    static constexpr int kACols = kKb * 32;  // one A stage in TMEM: 128 lanes x kKb K blocks of bf16 pairs
+    static constexpr int kAccBufs = NT == 64 ? 1 : 2;  // steps whose accumulators are in TMEM at once
+    static constexpr int kAccCols = kAccBufs * kKb * 2 * NT;
+    static constexpr int kAStages = (kDgTmemCols - kAccCols) / kACols;
+    static constexpr int kLoadStages = NT == 64 ? 4 : 6;
     static constexpr int kXBytes = NT * 128;                    // one bf16 [NT][64] tile
-    static constexpr int kXStage = 2 * kDgKb * kXBytes;        // [hi kb0 | lo kb0 | hi kb1 | lo kb1]
-    static constexpr int kCodeStage = kDgKb * kPgCodeBytes;     // [kb][128 rows][32 bytes]
+    static constexpr int kXStage = 2 * kKb * kXBytes;          // [hi kb0 | lo kb0 | hi kb1 | lo kb1 | ..]
+    static constexpr int kCodeStage = kKb * kPgCodeBytes;       // [kb][128 rows][32 bytes]
     static constexpr int kOffX = 0;
     static constexpr int kOffW = kOffX + kLoadStages * kXStage;
     static constexpr int kOffRed = kOffW + kLoadStages * kCodeStage;
@@ -493,7 +495,7 @@ struct DgCfg {
     static constexpr int kSmem = kOffBar + 512 + 1024;
     static_assert(kSmem <= 227 * 1024, "small-M GEMM shared memory");
     static_assert(kXBytes % 1024 == 0, "swizzle atoms");
-    static_assert(kAStages >= 2 && kAccCols + kAStages * kDgACols <= kDgTmemCols, "tensor memory budget");
+    static_assert(kAStages >= 2 && kAccCols + kAStages * kACols <= kDgTmemCols, "tensor memory budget");
 };
 
 // bf16x2 (128 + c0, 128 + c1) - (136, 136) = (c0 - 8, c1 - 8), exact.
@@ -540,7 +542,8 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
     const int mtiles = (p.M + NT - 1) / NT;
     const int tiles = mtiles * ((p.N + kPgRows - 1) / kPgRows);
     const int kblocks = p.K / kPgKb;
-    const int steps = kblocks / kDgKb;
+    constexpr int KB = C::kKb;
+    const int steps = kblocks / KB;
     const int st0 = static_cast<int>(rank * steps / S), st1 = static_cast<int>((rank + 1) * steps / S);
     const bool split = p.split != 0;
 
@@ -577,7 +580,7 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
     if (warp == 0) {
         // ---------------- producer (whole warp, one elected lane issues) ----------------
         uint32_t g = 0;
-        const uint32_t bytes = kDgKb * (split ? 2 : 1) * C::kXBytes + C::kCodeStage;
+        const uint32_t bytes = KB * (split ? 2 : 1) * C::kXBytes + C::kCodeStage;
         for (int tile = cid; tile < tiles; tile += ncl) {
             const int n0 = (tile / mtiles) * kPgRows, m0 = (tile % mtiles) * NT;
             for (int st = st0; st < st1; ++st, ++g) {
@@ -586,8 +589,8 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
                 uint8_t* xs = smem + C::kOffX + s * C::kXStage;
                 expect_tx_elect(&load_full[s], bytes);
 #pragma unroll
-                for (int j = 0; j < kDgKb; ++j) {
-                    const int kb = st * kDgKb + j;
+                for (int j = 0; j < KB; ++j) {
+                    const int kb = st * KB + j;
                     tma_2d_elect(xs + 2 * j * C::kXBytes, &p.map_x, kb * kPgKb, m0, &load_full[s]);
                     if (split) tma_2d_elect(xs + (2 * j + 1) * C::kXBytes, &p.map_x_lo, kb * kPgKb, m0, &load_full[s]);
                     tma_2d_elect(smem + C::kOffW + s * C::kCodeStage + j * kPgCodeBytes, &p.map_codes, kb * 32, n0,
@@ -620,10 +623,10 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t xa = smem_u32(smem + C::kOffX + s * C::kXStage);
-                const uint32_t aa = tmem + static_cast<uint32_t>(C::kAccCols + as * kDgACols);
+                const uint32_t aa = tmem + static_cast<uint32_t>(C::kAccCols + as * C::kACols);
 #pragma unroll
-                for (int j = 0; j < kDgKb; ++j) {
-                    const uint32_t d = tmem + static_cast<uint32_t>((b * kDgKb + j) * 2 * NT);
+                for (int j = 0; j < KB; ++j) {
+                    const uint32_t d = tmem + static_cast<uint32_t>((b * KB + j) * 2 * NT);
 #pragma unroll
                     for (int k = 0; k < kPgKb / 16; ++k)  // 16 K = 8 TMEM columns of A
                         tc_mma_ts_elect(d, aa + j * 32 + 8 * k, sw128_desc(xa + 2 * j * C::kXBytes + 32 * k), idesc,
@@ -640,7 +643,7 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
         __syncwarp();
     } else if (warp < 2 + kDgConvWarps) {
         // ---------------- code conversion (into the TMEM A stage) ----------------
-        const int q = warp & 3, j = (warp - 2) >> 2;  // TMEM lane quarter, K block of the step
+        const int q = warp & 3, j0 = (warp - 2) >> 2;  // TMEM lane quarter, first K block of the step
         const int row = 32 * q + lane;
         uint32_t g = 0;
         bool ok = true;
@@ -651,6 +654,8 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
                      (g < static_cast<uint32_t>(AS) || mbar_wait_bounded(&a_empty[as], ((g / AS) - 1) & 1, p.err, wait_ns));
                 if (!ok) break;
                 tc_fence_after();  // the MMAs that read this A stage have completed (a_empty)
+#pragma unroll 1
+                for (int j = j0; j < KB; j += 2) {
                 const uint8_t* cs = smem + C::kOffW + s * C::kCodeStage + j * kPgCodeBytes + row * 32;
                 const uint4 c0 = *reinterpret_cast<const uint4*>(cs);
                 const uint4 c1 = *reinterpret_cast<const uint4*>(cs + 16);
@@ -668,8 +673,9 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
                     a[4 * w + 3] = bf16x2_sub136(__byte_perm(c47, 0x43434343u, 0x4342));
                 }
                 tc_st32(tmem + (static_cast<uint32_t>(32 * q) << 16) +
-                            static_cast<uint32_t>(C::kAccCols + as * kDgACols + j * 32),
+                            static_cast<uint32_t>(C::kAccCols + as * C::kACols + j * 32),
                         a);
+                }
                 tc_wait_st();
                 tc_fence_before();
                 __syncwarp();
@@ -696,7 +702,7 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
             float acc[NH];
 #pragma unroll
             for (int j = 0; j < NH; ++j) acc[j] = 0.0f;
-            int gcur = (st0 * kDgKb) >> 3;
+            int gcur = (st0 * KB) >> 3;
             uint4 vcur = __ldg(reinterpret_cast<const uint4*>(meta + 16 * gcur));
             uint4 vnxt = __ldg(reinterpret_cast<const uint4*>(meta + 16 * min(gcur + 1, last_grp)));
             for (int st = st0; st < st1; ++st, ++g) {
@@ -705,8 +711,8 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
                 if (!ok) break;
                 tc_fence_after();
 #pragma unroll
-                for (int j = 0; j < kDgKb; ++j) {
-                    const int kb = st * kDgKb + j;
+                for (int j = 0; j < KB; ++j) {
+                    const int kb = st * KB + j;
                     if ((kb >> 3) != gcur) {  // next 8 groups' scales; the following 8 prefetched
                         gcur = kb >> 3;
                         vcur = vnxt;
@@ -714,7 +720,7 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
                     }
                     const float sc = scale_at(vcur, kb & 7);
                     const uint32_t ta = tmem + (static_cast<uint32_t>(32 * q) << 16) +
-                                        static_cast<uint32_t>((b * kDgKb + j) * 2 * NT + hcol * NH);
+                                        static_cast<uint32_t>((b * KB + j) * 2 * NT + hcol * NH);
                     constexpr int CH = NH > 16 ? 16 : NH;  // columns per TMEM load (register budget)
 #pragma unroll
                     for (int c0 = 0; c0 < NH; c0 += CH) {
@@ -863,7 +869,7 @@ cudaError_t launch_dg(const PgParams& p, int num_sms, cudaStream_t s) {
     });
     if (attr_err[dev] != cudaSuccess) return attr_err[dev];
     const int tiles = ((p.M + NT - 1) / NT) * ((p.N + kPgRows - 1) / kPgRows);
-    const int steps = p.K / (kPgKb * kDgKb);
+    const int steps = p.K / (kPgKb * C::kKb);
     static const int forced = env_int("XQ_GEMM_KSPLIT", 0);
     int best_s = 1, best_cl = std::max(1, fit[dev][1] ? fit[dev][1] : num_sms);
     long best = -1;
@@ -915,7 +921,7 @@ bool launch_prefill_gemm(const DevMatrix& w, const __nv_bfloat16* x, const __nv_
     // (32 by default: at M = 64 two 32-token tiles with two accumulators in flight measured up to
     // 1.3x faster per layer matrix than one 64-token tile, which has room for one)
     static const int small_nt_max = env_int("XQ_GEMM_SMALL_NT_MAX", 32);
-    const int small_nt = (!small_m_kernel || K % (kPgKb * kDgKb) != 0) ? 0
+    const int small_nt = (!small_m_kernel || K % (kPgKb * 4) != 0) ? 0
                          : M <= 16                                     ? 16
                          : M <= 32 || (small_nt_max < 64 && M <= 64)   ? std::min(32, std::max(16, small_nt_max))
                          : M <= 64                                     ? 64
