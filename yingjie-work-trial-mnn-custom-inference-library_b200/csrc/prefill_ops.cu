@@ -46,6 +46,49 @@ __global__ void rmsnorm_split_kernel(const float* H, const float* w, int n, floa
         store_split(hi, lo, static_cast<size_t>(t) * n + k, x[k] * inv * w[k]);
 }
 
+// The same for rows of at most 8192 floats (n % 4 == 0): every thread loads its float4s before
+// any arithmetic, so a row is one memory round trip instead of one per loop iteration.
+__global__ void __launch_bounds__(256) rmsnorm_split_vec_kernel(const float* H, const float* w, int n, float eps,
+                                                                __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    constexpr int kV = 8;  // float4s per thread held in registers
+    __shared__ float ws[8];
+    const int t = blockIdx.x, n4 = n >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(H + static_cast<size_t>(t) * n);
+    float4 v[kV];
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+        const int k = threadIdx.x + i * 256;
+        v[i] = k < n4 ? x4[k] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kV; ++i) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += ws[i];
+    const float inv = 1.0f / sqrtf(tot / static_cast<float>(n) + eps);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+        const int k = threadIdx.x + i * 256;
+        if (k >= n4) break;
+        const float4 g = w4[k];
+        const float o[4] = {v[i].x * inv * g.x, v[i].y * inv * g.y, v[i].z * inv * g.z, v[i].w * inv * g.w};
+        __nv_bfloat16 h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            h[j] = __float2bfloat16_rn(o[j]);
+            l[j] = __float2bfloat16_rn(o[j] - __bfloat162float(h[j]));
+        }
+        const size_t e = static_cast<size_t>(t) * n + 4 * static_cast<size_t>(k);
+        *reinterpret_cast<uint2*>(hi + e) = *reinterpret_cast<const uint2*>(h);
+        if (lo) *reinterpret_cast<uint2*>(lo + e) = *reinterpret_cast<const uint2*>(l);
+    }
+}
+
 // Causal conv1d + SiLU over the sequence, then the state shift (custom_model.cpp:985-1006,
 // conv_k = 4): one thread per channel walks the tokens in order. Y: [n][ldy] projections (the
 // first `channels` columns), out: [n][channels], state: [channels][3], updated in place.
@@ -340,12 +383,20 @@ __global__ void __launch_bounds__(1024) row_argmax_kernel(const float* logits, i
     const float* x = logits + static_cast<size_t>(blockIdx.x) * n;
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int k = threadIdx.x; k < n; k += blockDim.x) {
-        const float v = x[k];
-        if (v > bv) {  // k increases: a later equal value never replaces an earlier one
-            bv = v;
-            bi = k;
-        }
+    // eight loads in flight per thread, then compared in increasing k: a later equal value never
+    // replaces an earlier one
+    constexpr int kU = 8;
+    const int stride = blockDim.x;
+    for (int k0 = threadIdx.x; k0 < n; k0 += kU * stride) {
+        float v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) v[u] = k0 + u * stride < n ? x[k0 + u * stride] : -INFINITY;
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+            if (v[u] > bv) {
+                bv = v[u];
+                bi = k0 + u * stride;
+            }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -385,7 +436,13 @@ cudaError_t prefill_embed(const int* ids, const uint16_t* emb, float* H, int n, 
 
 cudaError_t prefill_rmsnorm_split(const float* H, const float* w, int n, int width, float eps, __nv_bfloat16* hi,
                                   __nv_bfloat16* lo, cudaStream_t s) {
-    rmsnorm_split_kernel<<<n, 256, 0, s>>>(H, w, width, eps, hi, lo);
+    const bool vec = width % 4 == 0 && width <= 8 * 1024 && (reinterpret_cast<uintptr_t>(H) & 15u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(w) & 15u) == 0 && (reinterpret_cast<uintptr_t>(hi) & 7u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(lo) & 7u) == 0;
+    if (vec)
+        rmsnorm_split_vec_kernel<<<n, 256, 0, s>>>(H, w, width, eps, hi, lo);
+    else
+        rmsnorm_split_kernel<<<n, 256, 0, s>>>(H, w, width, eps, hi, lo);
     return cudaGetLastError();
 }
 
