@@ -31,6 +31,8 @@ namespace {
 // pos[b] = next[b]++ (the position the step's forward writes), and the sampled tokens into the
 // ring at ring[(*ctr % ring_steps) * B + b].
 __global__ void batch_advance_kernel(const int* tokens, int* pos, int* next, int* ring, int* ctr, int ring_steps, int B) {
+    pdl_launch_dependents();  // programmatic dependent launch: inputs only after the
+    pdl_wait();               // previous kernel has finished
     const int b = threadIdx.x;
     const int k = *ctr;
     __syncthreads();
@@ -232,8 +234,8 @@ bool BatchModel::enqueue_step(cudaStream_t s, std::string* err) {
         !gemm(model_.lm_head(), logits_, d.vocab, kPgOutF32) ||
         !ok(batch_argmax(logits_, B_, d.vocab, tokens_, s), "argmax"))
         return false;
-    batch_advance_kernel<<<1, std::max(32, (B_ + 31) / 32 * 32), 0, s>>>(tokens_, pos_, next_, ring_, ring_ctr_,
-                                                                         ring_steps_, B_);
+    launch_ex(batch_advance_kernel, dim3(1), dim3(std::max(32, (B_ + 31) / 32 * 32)), 0, s, pdl_enabled(), tokens_, pos_,
+              next_, ring_, ring_ctr_, ring_steps_, B_);
     if (!ok(cudaGetLastError(), "advance") ||
         !ok(prefill_embed(tokens_, model_.embeddings(), H_, B_, d.hidden, d.vocab, s), "embedding"))
         return false;

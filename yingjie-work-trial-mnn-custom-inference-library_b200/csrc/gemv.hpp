@@ -79,6 +79,9 @@ bool launch_gemv_generic(const DevMatrix& m, const float* x, float* y, cudaStrea
 // Register the dynamic shared memory limits of every fused instantiation (once per device).
 bool gemv_init_device();
 
+// Programmatic dependent launch between kernels (XQ_PDL=0 turns it off, for A/B measurements).
+bool pdl_enabled();
+
 // Launch helper with the programmatic-dependent-launch attribute.
 template <typename Kernel, typename... Args>
 cudaError_t launch_ex(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,

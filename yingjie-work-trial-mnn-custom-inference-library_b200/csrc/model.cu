@@ -998,15 +998,6 @@ int DeviceModel::kernels_per_decode_step() const {
 
 int DeviceModel::kernels_per_prefill_step() const { return kernels_per_decode_step(); }
 
-// Programmatic dependent launch between the kernels of a step (XQ_PDL=0 turns it off, for
-// A/B measurements).
-static bool pdl_enabled() {
-    static const bool on = [] {
-        const char* e = std::getenv("XQ_PDL");
-        return !(e && std::atoi(e) == 0);
-    }();
-    return on;
-}
 
 bool DeviceModel::enqueue_forward(cudaStream_t s) {
     const ModelDims& d = d_;

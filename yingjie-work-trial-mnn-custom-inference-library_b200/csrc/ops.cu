@@ -51,6 +51,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_batch_kernel(const Att
                                                                       __nv_bfloat16* out_lo) {
     extern __shared__ float sm[];
     __shared__ AttnScratch sh;
+    pdl_launch_dependents();
+    pdl_wait();
     const int b = blockIdx.z;
     const size_t ob = static_cast<size_t>(b) * p.nq * p.hd;
     AttnParams q = p;
@@ -83,11 +85,10 @@ cudaError_t launch_attention_batch(const AttnParams& p, bool kv_fp16, size_t sme
     if (attr_err[dev] != cudaSuccess) return attr_err[dev];
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     const dim3 grid(p.nkv, kAttnSplits, batch), block(kAttnThreads);
-    if (kv_fp16)
-        attention_batch_kernel<__half><<<grid, block, smem, s>>>(p, qkv_stride, kv_bstride, out_hi, out_lo);
-    else
-        attention_batch_kernel<float><<<grid, block, smem, s>>>(p, qkv_stride, kv_bstride, out_hi, out_lo);
-    return cudaGetLastError();
+    return kv_fp16 ? launch_ex(attention_batch_kernel<__half>, grid, block, smem, s, pdl_enabled(), p, qkv_stride,
+                               kv_bstride, out_hi, out_lo)
+                   : launch_ex(attention_batch_kernel<float>, grid, block, smem, s, pdl_enabled(), p, qkv_stride,
+                               kv_bstride, out_hi, out_lo);
 }
 
 cudaError_t attention_init_device(int max_smem_bytes) {

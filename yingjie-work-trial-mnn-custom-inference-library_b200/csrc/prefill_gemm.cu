@@ -523,8 +523,9 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
     constexpr int LS = C::kLoadStages, AS = C::kAStages, RB = C::kAccBufs, NH = NT / 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* load_full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
-    uint64_t* load_empty = load_full + LS;
+    uint64_t* code_full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);  // raw codes of a load stage
+    uint64_t* x_full = code_full + LS;                                       // its X tiles
+    uint64_t* load_empty = x_full + LS;
     uint64_t* a_full = load_empty + LS;
     uint64_t* a_empty = a_full + AS;
     uint64_t* acc_full = a_empty + AS;
@@ -549,7 +550,8 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < LS; ++s) {
-            mbar_init(&load_full[s], 1);
+            mbar_init(&code_full[s], 1);
+            mbar_init(&x_full[s], 1);
             mbar_init(&load_empty[s], kDgConvWarps + 1);  // converter warps + the MMA commit
         }
         for (int s = 0; s < AS; ++s) {
@@ -576,35 +578,62 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
     tc_fence_after();
     if (S > 1) cluster_sync_all();  // the peers' barriers are initialised before any remote arrive
     const uint32_t tmem = *tmem_slot;
+    pdl_launch_dependents();  // the next kernel may be scheduled; it waits for this one itself
 
     if (warp == 0) {
         // ---------------- producer (whole warp, one elected lane issues) ----------------
-        uint32_t g = 0;
-        const uint32_t bytes = KB * (split ? 2 : 1) * C::kXBytes + C::kCodeStage;
-        for (int tile = cid; tile < tiles; tile += ncl) {
-            const int n0 = (tile / mtiles) * kPgRows, m0 = (tile % mtiles) * NT;
-            for (int st = st0; st < st1; ++st, ++g) {
-                const int s = g % LS;
-                if (g >= LS && !warp_wait(&load_empty[s], ((g / LS) - 1) & 1, p.err, wait_ns)) goto producer_done;
-                uint8_t* xs = smem + C::kOffX + s * C::kXStage;
-                expect_tx_elect(&load_full[s], bytes);
+        // The weight codes do not depend on the previous kernel in the stream: the first load
+        // stages' codes are requested before waiting for it (programmatic dependent launch), so
+        // the weight stream and the code conversion start during its tail; X only after.
+        const int per_tile = st1 - st0;
+        const int my_tiles = cid < tiles ? (tiles - 1 - cid) / ncl + 1 : 0;
+        const uint32_t total = static_cast<uint32_t>(per_tile * my_tiles);
+        const uint32_t xbytes = KB * (split ? 2 : 1) * C::kXBytes;
+        auto tile_of = [&](uint32_t g) { return cid + static_cast<int>(g / per_tile) * ncl; };
+        auto step_of = [&](uint32_t g) { return st0 + static_cast<int>(g % per_tile); };
+        auto issue_codes = [&](uint32_t g) {
+            const int s = g % LS, n0 = (tile_of(g) / mtiles) * kPgRows, st = step_of(g);
+            expect_tx_elect(&code_full[s], C::kCodeStage);
 #pragma unroll
-                for (int j = 0; j < KB; ++j) {
-                    const int kb = st * KB + j;
-                    tma_2d_elect(xs + 2 * j * C::kXBytes, &p.map_x, kb * kPgKb, m0, &load_full[s]);
-                    if (split) tma_2d_elect(xs + (2 * j + 1) * C::kXBytes, &p.map_x_lo, kb * kPgKb, m0, &load_full[s]);
-                    tma_2d_elect(smem + C::kOffW + s * C::kCodeStage + j * kPgCodeBytes, &p.map_codes, kb * 32, n0,
-                                 &load_full[s]);
-                }
+            for (int j = 0; j < KB; ++j)
+                tma_2d_elect(smem + C::kOffW + s * C::kCodeStage + j * kPgCodeBytes, &p.map_codes, (st * KB + j) * 32,
+                             n0, &code_full[s]);
+        };
+        auto issue_x = [&](uint32_t g) {
+            const int s = g % LS, m0 = (tile_of(g) % mtiles) * NT, st = step_of(g);
+            uint8_t* xs = smem + C::kOffX + s * C::kXStage;
+            expect_tx_elect(&x_full[s], xbytes);
+#pragma unroll
+            for (int j = 0; j < KB; ++j) {
+                const int kb = st * KB + j;
+                tma_2d_elect(xs + 2 * j * C::kXBytes, &p.map_x, kb * kPgKb, m0, &x_full[s]);
+                if (split) tma_2d_elect(xs + (2 * j + 1) * C::kXBytes, &p.map_x_lo, kb * kPgKb, m0, &x_full[s]);
             }
+        };
+        const uint32_t pre = total < static_cast<uint32_t>(LS) ? total : static_cast<uint32_t>(LS);
+        for (uint32_t g = 0; g < pre; ++g) issue_codes(g);
+        pdl_wait();
+        uint32_t gc = pre, gx = 0;
+        for (uint32_t g = 0; g < total; ++g) {
+            if (g >= pre) {
+                if (g >= static_cast<uint32_t>(LS) && !warp_wait(&load_empty[g % LS], ((g / LS) - 1) & 1, p.err, wait_ns))
+                    break;
+                issue_codes(g);
+                gc = g + 1;
+            }
+            issue_x(g);
+            gx = g + 1;
         }
-    producer_done:
-        for (uint32_t k = g > LS ? g - LS : 0; k < g; ++k) mbar_wait_drain(&load_full[k % LS], (k / LS) & 1);
+        // every issued copy lands before the CTA can exit (bounded, independent of errors)
+        for (uint32_t q = gc > static_cast<uint32_t>(LS) ? gc - LS : 0; q < gc; ++q)
+            mbar_wait_drain(&code_full[q % LS], (q / LS) & 1);
+        for (uint32_t q = gx > static_cast<uint32_t>(LS) ? gx - LS : 0; q < gx; ++q)
+            mbar_wait_drain(&x_full[q % LS], (q / LS) & 1);
         __syncwarp();
     } else if (warp == 1 || warp == 2 + kDgConvWarps + kDgAccWarps) {
         // ---------------- MMA issuers (whole warp, one elected lane issues) ----------------
         // warp 1 issues the even steps, the last warp the odd ones; each commits (and so tracks)
-        // only its own MMAs. a_full implies load_full: the converters waited for the stage.
+        // only its own MMAs.
         // With a single accumulator buffer one issuer could wait on acc_empty a full phase
         // ahead of the other, where a parity wait cannot tell the phases apart: warp 1 then
         // issues every step alone.
@@ -619,6 +648,7 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
                 if (return_role || (kTwoIssuers && (g & 1u) != parity)) continue;
                 const int s = g % LS, as = g % AS, b = g % RB;
                 ok = warp_wait(&a_full[as], (g / AS) & 1, p.err, wait_ns) &&
+                     warp_wait(&x_full[s], (g / LS) & 1, p.err, wait_ns) &&
                      (g < static_cast<uint32_t>(RB) || warp_wait(&acc_empty[b], ((g / RB) - 1) & 1, p.err, wait_ns));
                 if (!ok) break;
                 tc_fence_after();
@@ -650,7 +680,7 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
         for (int tile = cid; tile < tiles && ok; tile += ncl) {
             for (int st = st0; st < st1; ++st, ++g) {
                 const int s = g % LS, as = g % AS;
-                ok = mbar_wait_bounded(&load_full[s], (g / LS) & 1, p.err, wait_ns) &&
+                ok = mbar_wait_bounded(&code_full[s], (g / LS) & 1, p.err, wait_ns) &&
                      (g < static_cast<uint32_t>(AS) || mbar_wait_bounded(&a_empty[as], ((g / AS) - 1) & 1, p.err, wait_ns));
                 if (!ok) break;
                 tc_fence_after();  // the MMAs that read this A stage have completed (a_empty)
@@ -687,6 +717,7 @@ __global__ void __launch_bounds__(kDgThreads, 1) decode_gemm_kernel(const __grid
         }
     } else {
         // ---------------- accumulation + output ----------------
+        pdl_wait();  // y (added into, or overwritten) may be the previous kernel's
         const int q = warp & 3, hcol = (warp - 2 - kDgConvWarps) >> 2;
         const int rl = 32 * q + lane;  // tile row of this thread
         const int at = threadIdx.x - 32 * (2 + kDgConvWarps);  // 0..255
@@ -886,17 +917,19 @@ cudaError_t launch_dg(const PgParams& p, int num_sms, cudaStream_t s) {
         }
     }
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = best_s;
     at[0].val.clusterDim.y = 1;
     at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // weight codes before the wait
+    at[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(best_s * std::min(tiles, best_cl));
     cfg.blockDim = dim3(kDgThreads);
     cfg.dynamicSmemBytes = C::kSmem;
     cfg.stream = s;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, decode_gemm_kernel<NT>, p);
 }
 

@@ -6,12 +6,22 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "gemv.hpp"
 #include "ops_device.cuh"
 #include "prefill_ops.hpp"
 
 namespace xqb {
 
 namespace {
+
+// Every kernel of this file waits for its predecessor with griddepcontrol.wait before touching
+// memory, so all are launched with the programmatic-dependent-launch attribute: the launch and
+// block scheduling overlap the previous kernel's tail, and a following tensor-core GEMM can
+// start streaming its weights.
+template <typename Kernel, typename... Args>
+cudaError_t pdl_launch(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    return launch_ex(kernel, grid, block, smem, s, pdl_enabled(), args...);
+}
 
 __device__ __forceinline__ void store_split(__nv_bfloat16* hi, __nv_bfloat16* lo, size_t i, float v) {
     const __nv_bfloat16 h = __float2bfloat16_rn(v);
@@ -21,6 +31,8 @@ __device__ __forceinline__ void store_split(__nv_bfloat16* hi, __nv_bfloat16* lo
 
 // H[t] = embedding row of ids[t] (ids folded by abs % vocab, custom_model.cpp:573-575).
 __global__ void embed_rows_kernel(const int* ids, const uint16_t* emb, float* H, int hidden, int vocab) {
+    pdl_launch_dependents();  // launched with programmatic dependent launch: inputs only after
+    pdl_wait();               // the previous kernel has finished
     const int t = blockIdx.x;
     long long id = ids[t];
     if (id < 0 || id >= vocab) id = (id < 0 ? -id : id) % (vocab > 1 ? vocab : 1);
@@ -31,6 +43,8 @@ __global__ void embed_rows_kernel(const int* ids, const uint16_t* emb, float* H,
 // X[t] = rmsnorm(H[t]) * w as a bf16 pair (rmsnormReference, ref_rmsnorm.cpp:8-17). 256 threads.
 __global__ void rmsnorm_split_kernel(const float* H, const float* w, int n, float eps, __nv_bfloat16* hi,
                                      __nv_bfloat16* lo) {
+    pdl_launch_dependents();  // launched with programmatic dependent launch: inputs only after
+    pdl_wait();               // the previous kernel has finished
     __shared__ float ws[8];
     const int t = blockIdx.x;
     const float* x = H + static_cast<size_t>(t) * n;
@@ -50,6 +64,8 @@ __global__ void rmsnorm_split_kernel(const float* H, const float* w, int n, floa
 // any arithmetic, so a row is one memory round trip instead of one per loop iteration.
 __global__ void __launch_bounds__(256) rmsnorm_split_vec_kernel(const float* H, const float* w, int n, float eps,
                                                                 __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    pdl_launch_dependents();  // launched with programmatic dependent launch: inputs only after
+    pdl_wait();               // the previous kernel has finished
     constexpr int kV = 8;  // float4s per thread held in registers
     __shared__ float ws[8];
     const int t = blockIdx.x, n4 = n >> 2;
@@ -96,6 +112,8 @@ __global__ void __launch_bounds__(256) rmsnorm_split_vec_kernel(const float* H, 
 // (batched decode: n = 1 per sequence).
 __global__ void conv_seq_kernel(const float* Y, int ldy, const float* w, float* state, float* out, int n, int channels,
                                 size_t state_bstride) {
+    pdl_launch_dependents();  // launched with programmatic dependent launch: inputs only after
+    pdl_wait();               // the previous kernel has finished
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= channels) return;
     Y += static_cast<size_t>(blockIdx.y) * n * ldy;
@@ -129,6 +147,8 @@ __global__ void __launch_bounds__(128) delta_seq_kernel(const float* conv, int c
                                                         int ab_off, const float* a_log_p, const float* dt_bias_p,
                                                         float* state, float* out, int out_ld, int n, int nk, int nv,
                                                         int dk, int dv, size_t state_bstride) {
+    pdl_launch_dependents();  // launched with programmatic dependent launch: inputs only after
+    pdl_wait();               // the previous kernel has finished
     __shared__ DeltaScratch sh;
     conv += static_cast<size_t>(blockIdx.z) * n * conv_ld;
     Y += static_cast<size_t>(blockIdx.z) * n * ldy;
@@ -225,6 +245,8 @@ __global__ void __launch_bounds__(128) delta_seq_kernel(const float* conv, int c
 // without +1) of token t, head h, as a bf16 pair. One warp per (t, head), head_dim 128.
 __global__ void gated_norm_split_kernel(const float* O, int o_ld, const float* Y, int ldy, int z_off, const float* w,
                                         int heads, int hd, float eps, int n, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    pdl_launch_dependents();  // launched with programmatic dependent launch: inputs only after
+    pdl_wait();               // the previous kernel has finished
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (gw >= n * heads) return;
     const int t = gw / heads, h = gw % heads;
@@ -248,6 +270,8 @@ template <typename KV>
 __global__ void attn_prep_kernel(const float* Y, int ldy, const float* q_norm, const float* k_norm, const float2* rope,
                                  int rope_stride, float* Q, KV* kc, KV* vc, int p0, int n, int nq, int nkv, int hd,
                                  float eps, const int* pos_arr, size_t kv_bstride) {
+    pdl_launch_dependents();  // launched with programmatic dependent launch: inputs only after
+    pdl_wait();               // the previous kernel has finished
     const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (gw >= n * (nq + nkv)) return;
     const int t = gw / (nq + nkv), h = gw % (nq + nkv);
@@ -293,6 +317,8 @@ __global__ void __launch_bounds__(256) attn_causal_kernel(const float* Q, const 
                                                           const KV* vc, int p0, int nq, int nkv, int hd,
                                                           __nv_bfloat16* hi, __nv_bfloat16* lo, const int* pos_arr,
                                                           size_t kv_bstride) {
+    pdl_launch_dependents();  // launched with programmatic dependent launch: inputs only after
+    pdl_wait();               // the previous kernel has finished
     extern __shared__ float dyn[];
     const int t = blockIdx.x, kh = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -368,6 +394,8 @@ __global__ void __launch_bounds__(256) attn_causal_kernel(const float* Q, const 
 
 // SwiGLU of the interleaved gate/up rows (custom_model.cpp:1226-1230) as a bf16 pair.
 __global__ void swiglu_split_kernel(const float* Y, int ldy, int inter, int n, __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    pdl_launch_dependents();  // launched with programmatic dependent launch: inputs only after
+    pdl_wait();               // the previous kernel has finished
     const size_t e = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (e >= static_cast<size_t>(n) * inter) return;
     const size_t t = e / inter, j = e % inter;
@@ -378,6 +406,8 @@ __global__ void swiglu_split_kernel(const float* Y, int ldy, int inter, int n, _
 // Row argmax, ties to the lowest index (gemvW4A16ArgmaxNeon, xq_gemv_w4a16_neon.cpp:315-318): one
 // block of 1024 threads per row. A NaN never wins (as with the reference's `>` comparisons).
 __global__ void __launch_bounds__(1024) row_argmax_kernel(const float* logits, int n, int* idx) {
+    pdl_launch_dependents();  // launched with programmatic dependent launch: inputs only after
+    pdl_wait();               // the previous kernel has finished
     __shared__ float sv[32];
     __shared__ int si[32];
     const float* x = logits + static_cast<size_t>(blockIdx.x) * n;
@@ -425,12 +455,12 @@ __global__ void __launch_bounds__(1024) row_argmax_kernel(const float* logits, i
 }  // namespace
 
 cudaError_t batch_argmax(const float* logits, int rows, int n, int* idx, cudaStream_t s) {
-    row_argmax_kernel<<<rows, 1024, 0, s>>>(logits, n, idx);
+    pdl_launch(row_argmax_kernel, dim3(rows), dim3(1024), 0, s, logits, n, idx);
     return cudaGetLastError();
 }
 
 cudaError_t prefill_embed(const int* ids, const uint16_t* emb, float* H, int n, int hidden, int vocab, cudaStream_t s) {
-    embed_rows_kernel<<<n, 256, 0, s>>>(ids, emb, H, hidden, vocab);
+    pdl_launch(embed_rows_kernel, dim3(n), dim3(256), 0, s, ids, emb, H, hidden, vocab);
     return cudaGetLastError();
 }
 
@@ -440,15 +470,15 @@ cudaError_t prefill_rmsnorm_split(const float* H, const float* w, int n, int wid
                      (reinterpret_cast<uintptr_t>(w) & 15u) == 0 && (reinterpret_cast<uintptr_t>(hi) & 7u) == 0 &&
                      (reinterpret_cast<uintptr_t>(lo) & 7u) == 0;
     if (vec)
-        rmsnorm_split_vec_kernel<<<n, 256, 0, s>>>(H, w, width, eps, hi, lo);
+        pdl_launch(rmsnorm_split_vec_kernel, dim3(n), dim3(256), 0, s, H, w, width, eps, hi, lo);
     else
-        rmsnorm_split_kernel<<<n, 256, 0, s>>>(H, w, width, eps, hi, lo);
+        pdl_launch(rmsnorm_split_kernel, dim3(n), dim3(256), 0, s, H, w, width, eps, hi, lo);
     return cudaGetLastError();
 }
 
 cudaError_t prefill_conv(const float* Y, int ldy, const float* w, float* state, float* out, int n, int channels,
                          cudaStream_t s, int nseq, size_t state_bstride) {
-    conv_seq_kernel<<<dim3((channels + 127) / 128, nseq), 128, 0, s>>>(Y, ldy, w, state, out, n, channels,
+    pdl_launch(conv_seq_kernel, dim3(dim3((channels + 127) / 128, nseq)), dim3(128), 0, s, Y, ldy, w, state, out, n, channels,
                                                                       state_bstride);
     return cudaGetLastError();
 }
@@ -457,7 +487,7 @@ cudaError_t prefill_delta(const float* conv, int conv_ld, const float* Y, int ld
                           const float* dt_bias, float* state, float* out, int out_ld, int n, int nk, int nv, int dk,
                           int dv, cudaStream_t s, int nseq, size_t state_bstride) {
     if (dk != 128 || dv % kDeltaCols != 0) return cudaErrorInvalidValue;
-    delta_seq_kernel<<<dim3(nv, dv / kDeltaCols, nseq), 128, 0, s>>>(conv, conv_ld, Y, ldy, ab_off, a_log, dt_bias,
+    pdl_launch(delta_seq_kernel, dim3(dim3(nv, dv / kDeltaCols, nseq)), dim3(128), 0, s, conv, conv_ld, Y, ldy, ab_off, a_log, dt_bias,
                                                                       state, out, out_ld, n, nk, nv, dk, dv,
                                                                       state_bstride);
     return cudaGetLastError();
@@ -466,7 +496,7 @@ cudaError_t prefill_delta(const float* conv, int conv_ld, const float* Y, int ld
 cudaError_t prefill_gated_norm(const float* O, int o_ld, const float* Y, int ldy, int z_off, const float* w, int heads,
                                int hd, float eps, int n, __nv_bfloat16* hi, __nv_bfloat16* lo, cudaStream_t s) {
     const int warps = n * heads;
-    gated_norm_split_kernel<<<(warps + 7) / 8, 256, 0, s>>>(O, o_ld, Y, ldy, z_off, w, heads, hd, eps, n, hi, lo);
+    pdl_launch(gated_norm_split_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, O, o_ld, Y, ldy, z_off, w, heads, hd, eps, n, hi, lo);
     return cudaGetLastError();
 }
 
@@ -476,11 +506,11 @@ cudaError_t prefill_attn_prep(const float* Y, int ldy, const float* q_norm, cons
     if (hd != 256) return cudaErrorInvalidValue;
     const int warps = n * (nq + nkv);
     if (kv_fp16)
-        attn_prep_kernel<__half><<<(warps + 7) / 8, 256, 0, s>>>(Y, ldy, q_norm, k_norm, rope, rope_stride, Q,
+        pdl_launch(attn_prep_kernel<__half>, dim3((warps + 7) / 8), dim3(256), 0, s, Y, ldy, q_norm, k_norm, rope, rope_stride, Q,
                                                                 static_cast<__half*>(kc), static_cast<__half*>(vc), p0,
                                                                 n, nq, nkv, hd, eps, pos_arr, kv_bstride);
     else
-        attn_prep_kernel<float><<<(warps + 7) / 8, 256, 0, s>>>(Y, ldy, q_norm, k_norm, rope, rope_stride, Q,
+        pdl_launch(attn_prep_kernel<float>, dim3((warps + 7) / 8), dim3(256), 0, s, Y, ldy, q_norm, k_norm, rope, rope_stride, Q,
                                                                static_cast<float*>(kc), static_cast<float*>(vc), p0, n,
                                                                nq, nkv, hd, eps, pos_arr, kv_bstride);
     return cudaGetLastError();
@@ -502,14 +532,14 @@ cudaError_t prefill_attn(const float* Q, const float* Y, int ldy, const void* kc
         e = cudaFuncSetAttribute(attn_causal_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kPrefillAttnMaxSmem);
         if (e != cudaSuccess) return e;
-        attn_causal_kernel<__half><<<dim3(n, nkv), 256, smem, s>>>(Q, Y, ldy, static_cast<const __half*>(kc),
+        pdl_launch(attn_causal_kernel<__half>, dim3(dim3(n, nkv)), dim3(256), smem, s, Q, Y, ldy, static_cast<const __half*>(kc),
                                                                    static_cast<const __half*>(vc), p0, nq, nkv, hd, hi,
                                                                    lo, pos_arr, kv_bstride);
     } else {
         e = cudaFuncSetAttribute(attn_causal_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  kPrefillAttnMaxSmem);
         if (e != cudaSuccess) return e;
-        attn_causal_kernel<float><<<dim3(n, nkv), 256, smem, s>>>(Q, Y, ldy, static_cast<const float*>(kc),
+        pdl_launch(attn_causal_kernel<float>, dim3(dim3(n, nkv)), dim3(256), smem, s, Q, Y, ldy, static_cast<const float*>(kc),
                                                                   static_cast<const float*>(vc), p0, nq, nkv, hd, hi,
                                                                   lo, pos_arr, kv_bstride);
     }
@@ -519,7 +549,7 @@ cudaError_t prefill_attn(const float* Q, const float* Y, int ldy, const void* kc
 cudaError_t prefill_swiglu(const float* Y, int ldy, int inter, int n, __nv_bfloat16* hi, __nv_bfloat16* lo,
                            cudaStream_t s) {
     const size_t total = static_cast<size_t>(n) * inter;
-    swiglu_split_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(Y, ldy, inter, n, hi, lo);
+    pdl_launch(swiglu_split_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0, s, Y, ldy, inter, n, hi, lo);
     return cudaGetLastError();
 }
 

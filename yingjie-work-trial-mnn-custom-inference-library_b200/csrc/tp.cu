@@ -170,6 +170,8 @@ HostMatrix slice_cols(const HostMatrix& m, int c0, int c1) {
 // x[t] = rmsnorm(H[t] (+= P[t] first when P is given)) * w as a bf16 pair; one block, 1024 threads.
 __global__ void __launch_bounds__(1024) tp_add_norm_split_kernel(float* H, const float* P, const float* w, int n, float eps,
                                                                  __nv_bfloat16* hi, __nv_bfloat16* lo) {
+    pdl_launch_dependents();  // programmatic dependent launch: inputs only after the
+    pdl_wait();               // previous kernel has finished
     __shared__ float ws[32];
     float ss = 0.0f;
     for (int k = threadIdx.x; k < n; k += blockDim.x) {
@@ -195,6 +197,8 @@ __global__ void __launch_bounds__(1024) tp_add_norm_split_kernel(float* H, const
 }
 
 __global__ void tp_add_kernel(float* H, const float* P, int n) {
+    pdl_launch_dependents();  // programmatic dependent launch: inputs only after the
+    pdl_wait();               // previous kernel has finished
     const int k = blockIdx.x * blockDim.x + threadIdx.x;
     if (k < n) H[k] += P[k];
 }
@@ -202,6 +206,8 @@ __global__ void tp_add_kernel(float* H, const float* P, int n) {
 // (max, lowest index) of this rank's logits, the index offset to the global vocabulary; the
 // pair is written as two 32-bit words (value bits, index) for the all-gather.
 __global__ void __launch_bounds__(1024) tp_local_argmax_kernel(const float* logits, int n, int offset, int* pair) {
+    pdl_launch_dependents();  // programmatic dependent launch: inputs only after the
+    pdl_wait();               // previous kernel has finished
     __shared__ float sv[32];
     __shared__ int si[32];
     float bv = -INFINITY;
@@ -240,6 +246,8 @@ __global__ void __launch_bounds__(1024) tp_local_argmax_kernel(const float* logi
 // pos = next++, token into the ring.
 __global__ void tp_pick_kernel(const int* pairs, int world, int* token, int* pos, int* next, int* ring, int* ctr,
                                int ring_steps) {
+    pdl_launch_dependents();  // programmatic dependent launch: inputs only after the
+    pdl_wait();               // previous kernel has finished
     if (threadIdx.x != 0) return;
     float bv = -INFINITY;
     int bi = INT_MAX;
@@ -567,7 +575,7 @@ bool TpModel::enqueue_forward(cudaStream_t s, std::string* err) {
         return false;
     };
     auto norm = [&](const float* P, const float* w) {
-        tp_add_norm_split_kernel<<<1, 1024, 0, s>>>(H_, P, w, d.hidden, d.eps, xhi_, xlo_);
+        launch_ex(tp_add_norm_split_kernel, dim3(1), dim3(1024), 0, s, pdl_enabled(), H_, P, w, d.hidden, d.eps, xhi_, xlo_);
         return ok(cudaGetLastError(), "norm");
     };
     if (!ok(prefill_embed(tok_, emb_, H_, 1, d.hidden, d.vocab, s), "embedding")) return false;
@@ -616,7 +624,7 @@ bool TpModel::enqueue_forward(cudaStream_t s, std::string* err) {
             !gemm(L.down, P_, d.hidden) || !all_reduce(P_))
             return false;
     }
-    tp_add_kernel<<<(d.hidden + 255) / 256, 256, 0, s>>>(H_, P_, d.hidden);
+    launch_ex(tp_add_kernel, dim3((d.hidden + 255) / 256), dim3(256), 0, s, pdl_enabled(), H_, P_, d.hidden);
     return ok(cudaGetLastError(), "residual");
 }
 
@@ -624,18 +632,18 @@ bool TpModel::enqueue_forward(cudaStream_t s, std::string* err) {
 // then pos_ = next_++.
 bool TpModel::enqueue_sample(cudaStream_t s, std::string* err) {
     const ModelDims& d = d_;
-    tp_add_norm_split_kernel<<<1, 1024, 0, s>>>(H_, nullptr, final_norm_, d.hidden, d.eps, xhi_, xlo_);
+    launch_ex(tp_add_norm_split_kernel, dim3(1), dim3(1024), 0, s, pdl_enabled(), H_, nullptr, final_norm_, d.hidden, d.eps, xhi_, xlo_);
     if (!launch_prefill_gemm(lm_head_, xhi_, xlo_, 1, logits_, vocab_, kPgOutF32, err_, 148, s)) {
         *err = std::string("tensor parallel: ") + last_error();
         return false;
     }
-    tp_local_argmax_kernel<<<1, 1024, 0, s>>>(logits_, vocab_, plan_.t0, pair_);
+    launch_ex(tp_local_argmax_kernel, dim3(1), dim3(1024), 0, s, pdl_enabled(), logits_, vocab_, plan_.t0, pair_);
     const ncclResult_t r = nccl().all_gather(pair_, pairs_, 2, ncclInt32, comm_, s);
     if (r != ncclSuccess) {
         *err = "tensor parallel: ncclAllGather failed: " + nccl_error(r);
         return false;
     }
-    tp_pick_kernel<<<1, 32, 0, s>>>(pairs_, plan_.world, tok_, pos_, next_, ring_, ring_ctr_, ring_steps_);
+    launch_ex(tp_pick_kernel, dim3(1), dim3(32), 0, s, pdl_enabled(), pairs_, plan_.world, tok_, pos_, next_, ring_, ring_ctr_, ring_steps_);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         *err = std::string("tensor parallel: sample: ") + cudaGetErrorString(e);
