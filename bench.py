@@ -561,8 +561,11 @@ def main():
     tp = None
     if world > 1 and not args.no_tp:
         tp_ids = np.random.default_rng(SEED).integers(0, 248320, args.prompt).astype(np.int32)
-        tp = tp_decode(pkg, d, rank, world, local, tp_ids, args.steps, args.warmup, args.kv_fp16,
-                       32 if args.preset == "cfg2" else 2)
+        try:  # a shape that does not split evenly fails the same way on every rank, before NCCL
+            tp = tp_decode(pkg, d, rank, world, local, tp_ids, args.steps, args.warmup, args.kv_fp16,
+                           32 if args.preset == "cfg2" else 2)
+        except (RuntimeError, ValueError) as e:
+            tp = {"error": str(e)[:300]}
 
     info = json.loads(sess.json("backend"))
     if os.environ.get("XQ_STEP_TRACE") and rank == 0 and info.get("step_phase_trace"):
