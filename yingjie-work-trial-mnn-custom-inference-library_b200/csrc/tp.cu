@@ -167,32 +167,56 @@ HostMatrix slice_cols(const HostMatrix& m, int c0, int c1) {
     return o;
 }
 
-// x[t] = rmsnorm(H[t] (+= P[t] first when P is given)) * w as a bf16 pair; one block, 1024 threads.
+// x = rmsnorm(H (+= P first when P is given)) * w as a bf16 pair; one block of 1024 threads, each
+// holding up to two float4s of the row in registers (hidden <= 8192, a multiple of 4), so the
+// row is read in one memory round trip.
 __global__ void __launch_bounds__(1024) tp_add_norm_split_kernel(float* H, const float* P, const float* w, int n, float eps,
                                                                  __nv_bfloat16* hi, __nv_bfloat16* lo) {
     pdl_launch_dependents();  // programmatic dependent launch: inputs only after the
     pdl_wait();               // previous kernel has finished
+    constexpr int kV = 2;
     __shared__ float ws[32];
-    float ss = 0.0f;
-    for (int k = threadIdx.x; k < n; k += blockDim.x) {
-        float x = H[k];
-        if (P) {
-            x += P[k];
-            H[k] = x;
+    const int n4 = n >> 2;
+    float4* h4 = reinterpret_cast<float4*>(H);
+    const float4* p4 = reinterpret_cast<const float4*>(P);
+    float4 v[kV];
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+        const int k = threadIdx.x + i * 1024;
+        v[i] = k < n4 ? h4[k] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (P && k < n4) {
+            const float4 q = p4[k];
+            v[i].x += q.x;
+            v[i].y += q.y;
+            v[i].z += q.z;
+            v[i].w += q.w;
+            h4[k] = v[i];
         }
-        ss += x * x;
     }
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kV; ++i) ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = ss;
     __syncthreads();
     float tot = 0.0f;
     for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) tot += ws[i];
     const float inv = 1.0f / sqrtf(tot / static_cast<float>(n) + eps);
-    for (int k = threadIdx.x; k < n; k += blockDim.x) {
-        const float v = H[k] * inv * w[k];
-        const __nv_bfloat16 h = __float2bfloat16_rn(v);
-        hi[k] = h;
-        lo[k] = __float2bfloat16_rn(v - __bfloat162float(h));
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+        const int k = threadIdx.x + i * 1024;
+        if (k >= n4) break;
+        const float4 g = w4[k];
+        const float o[4] = {v[i].x * inv * g.x, v[i].y * inv * g.y, v[i].z * inv * g.z, v[i].w * inv * g.w};
+        __nv_bfloat16 hh[4], ll[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            hh[j] = __float2bfloat16_rn(o[j]);
+            ll[j] = __float2bfloat16_rn(o[j] - __bfloat162float(hh[j]));
+        }
+        *reinterpret_cast<uint2*>(hi + 4 * k) = *reinterpret_cast<const uint2*>(hh);
+        *reinterpret_cast<uint2*>(lo + 4 * k) = *reinterpret_cast<const uint2*>(ll);
     }
 }
 
@@ -466,9 +490,9 @@ bool TpModel::create(const std::string& dir, const Options& opts, int world, int
         return false;
     }
     if (d.head_dim != kAttnThreads || d.rotary_dim != 64 || d.lk_hd != 128 || d.lv_hd % kDeltaCols != 0 ||
-        d.conv_k != 4 || d.hidden % 512 != 0) {
+        d.conv_k != 4 || d.hidden % 512 != 0 || d.hidden > 8192) {
         *err = "tensor parallel decode serves the fused shapes only (head_dim 256, rotary 64, DeltaNet key dim 128, "
-               "conv kernel 4)";
+               "conv kernel 4, hidden a multiple of 512 up to 8192)";
         return false;
     }
     if (!nccl().ok) {
