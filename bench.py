@@ -153,7 +153,7 @@ def step_roofline(alg_bytes, ms_per_step, peak_gbs):
             "launch_us": round(ms_per_step * 1000, 2)}
 
 
-def gemv_roofline(pkg, peak_gbs, iters=40, engine="dp4a", rows=24576, cols=4096):
+def gemv_roofline(pkg, peak_gbs, iters=40, engine="dp4a", rows=24576, cols=4096, max_copies=4):
     """A standalone W4A16 GEMV kernel of the kernel-level C ABI, timed with CUDA events on the
     launching stream: engine "dp4a" (gemv_w4a16_kernel, also the per-op path) or "mma" (the
     tensor-core gemv_mma_kernel, xqk_gemv_w4a16_mma). The default shape is the largest
@@ -162,7 +162,7 @@ def gemv_roofline(pkg, peak_gbs, iters=40, engine="dp4a", rows=24576, cols=4096)
     import torch
 
     one = rows * cols // 2 + rows * (cols // 64) * 2
-    ncopy = max(1, min(4, -(-200_000_000 // one)))
+    ncopy = max(1, min(max_copies, -(-200_000_000 // one)))
     mats = []
     for i in range(ncopy):
         rng = np.random.default_rng(100 + i)
@@ -194,6 +194,40 @@ def gemv_roofline(pkg, peak_gbs, iters=40, engine="dp4a", rows=24576, cols=4096)
             "frac": round(achieved / peak_gbs, 4),
             "kernel": "gemv_mma_kernel" if engine == "mma" else "gemv_w4a16_kernel",
             "shape": f"{rows}x{cols}", "algorithmic_bytes": alg, "launch_us": round(ms * 1000, 2)}
+
+
+def gemv_fixed_cost(pkg, peak_gbs):
+    """Where a standalone tensor-core GEMV (xqk_gemv_w4a16_mma) spends the time its bytes do not
+    explain: the same kernel at three row counts (K = 4096), each rotating over weight copies
+    that together exceed L2, a least-squares fit of launch time = fixed + bytes / rate, and, as
+    the floor of back-to-back launches on this stream, a one-element torch kernel timed the same
+    way."""
+    import torch
+
+    pts = []
+    for rows in (2368, 24576, 248320):  # 2368 = 148 blocks x 16 rows: one tile per block
+        r = gemv_roofline(pkg, peak_gbs, iters=80, engine="mma", rows=rows, max_copies=48)
+        pts.append((r["algorithmic_bytes"], r["launch_us"]))
+    a = np.array([[1.0, b / 1e9] for b, _ in pts])
+    fixed, per_gb = np.linalg.lstsq(a, np.array([t for _, t in pts]), rcond=None)[0]
+    z = torch.zeros(1, device="cuda")
+    st = torch.cuda.current_stream()
+    for _ in range(10):
+        z.add_(1.0)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(200):
+        z.add_(1.0)
+    e1.record(st)
+    torch.cuda.synchronize()
+    empty_us = e0.elapsed_time(e1) * 1000 / 200
+    return {"kernel": "gemv_mma_kernel", "cols": 4096,
+            "points": [{"algorithmic_bytes": b, "launch_us": t} for b, t in pts],
+            "fit_fixed_us": round(float(fixed), 2), "fit_stream_gb_s": round(1e6 / float(per_gb), 1),
+            "empty_launch_us": round(empty_us, 2),
+            "note": "launch time = fixed + bytes / stream rate over 2368, 24576 and 248320 rows; "
+                    "empty_launch_us: back-to-back one-element kernels on the same stream"}
 
 
 def config0_gemv(pkg, peak_gbs, iters=200):
@@ -490,6 +524,8 @@ def main():
     ap.add_argument("--gemm-only", default=None, metavar="M,K,N",
                     help="time only the prefill GEMM at one config-3 shape (profiling runs), print its point")
     ap.add_argument("--gemm-split", action="store_true", help="with --gemm-only: the split-bf16 mode")
+    ap.add_argument("--gemv-cost-only", action="store_true",
+                    help="only the standalone GEMV's fixed-cost fit (gemv_fixed_cost)")
     ap.add_argument("--batch-only", type=int, default=0, metavar="B",
                     help="time only batched decode (config 4) at batch B, --steps steps (profiling runs)")
     ap.add_argument("--preset", default="cfg2", choices=["cfg2", "small"],
@@ -497,6 +533,12 @@ def main():
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
+    if args.gemv_cost_only:
+        pkg = __graft_entry__.load_package()
+        import torch
+        torch.cuda.set_device(0)
+        print(json.dumps(gemv_fixed_cost(pkg, peaks()[0])), flush=True)
+        return 0
     if args.gemm_only:
         M, K, N = (int(v) for v in args.gemm_only.split(","))
         pkg = __graft_entry__.load_package()
@@ -589,6 +631,7 @@ def main():
     # the per-config lines run at N = 1 (at N > 1 the job measures replicas and tensor parallel)
     extra = world == 1 and not args.no_extra
     cfg0 = config0_gemv(pkg, peak) if extra else None
+    gemv_cost = gemv_fixed_cost(pkg, peak) if extra else None
     cfg3 = config3_sweep(pkg, bf16_peak()) if extra else None
     cfg4 = config4_batched(pkg, d, peak, info.get("weight_bytes", 0), kv_fp16=args.kv_fp16) \
         if extra and args.preset == "cfg2" else None
@@ -626,6 +669,7 @@ def main():
             "gemv_kernels": [dict(g, peak_kind=peak_kind) for g in gemvs] if gemvs else None,
             "prefill_batched_tok_s": prefill_batched,
             "config0_gemv": cfg0,
+            "gemv_fixed_cost": gemv_cost,
             "config3_gemm": cfg3,
             "config4_batched_decode": cfg4,
             "config1_step": cfg1,
