@@ -167,14 +167,14 @@ __device__ __forceinline__ void norm_rope_head(float (&v)[8], const float* w, in
 // Split-K flash decode of one (kv head, split) item: score positions [t0, t1) of kv head kh
 // for all its query heads, keep (max, sum, unnormalised output) per head; the last item of a
 // kv head to finish merges the splits and applies the sigmoid output gate.
-template <typename KV>
+template <typename KV, int SPLITS = kAttnSplits>
 __device__ __forceinline__ void attention_item(const AttnParams& p, int kh, int split, int tid, int bar_id, float* dyn,
                                AttnScratch* sh, __nv_bfloat16* out_hi = nullptr,
                                __nv_bfloat16* out_lo = nullptr) {
     const int lane = tid & 31, warp = tid >> 5;
     const int hd = p.hd;
     const int group = p.nq / p.nkv;
-    const int cmax = (p.capacity + kAttnSplits - 1) / kAttnSplits;
+    const int cmax = (p.capacity + SPLITS - 1) / SPLITS;
     float* qs = dyn;               // [group][hd]
     float* sc = dyn + group * hd;  // [group][cmax]
     KV* kc = static_cast<KV*>(p.k_cache);
@@ -182,7 +182,7 @@ __device__ __forceinline__ void attention_item(const AttnParams& p, int kh, int 
 
     const int pos = p.pos_ptr ? __ldcg(p.pos_ptr) : p.pos_const;
     const int L = pos + 1;
-    const int chunk = (L + kAttnSplits - 1) / kAttnSplits;
+    const int chunk = (L + SPLITS - 1) / SPLITS;
     const int t0 = min(L, split * chunk);
     const int t1 = min(L, t0 + chunk);
     const int n = t1 - t0;
@@ -276,7 +276,7 @@ __device__ __forceinline__ void attention_item(const AttnParams& p, int kh, int 
                     if (g < group) o[g] += sc[g * cmax + j0 + u] * vb[u];
             }
     }
-    float* pp = p.part + static_cast<size_t>(kh * kAttnSplits + split) * group * (hd + 2);
+    float* pp = p.part + static_cast<size_t>(kh * SPLITS + split) * group * (hd + 2);
 #pragma unroll
     for (int g = 0; g < kAttnMaxGroup; ++g)
         if (g < group) pp[g * (hd + 2) + tid] = o[g];
@@ -286,18 +286,18 @@ __device__ __forceinline__ void attention_item(const AttnParams& p, int kh, int 
     }
     __threadfence();
     bar_sync(bar_id, kAttnThreads);
-    if (tid == 0) sh->last = (atomicAdd(&p.counters[kh], 1u) == kAttnSplits - 1) ? 1 : 0;
+    if (tid == 0) sh->last = (atomicAdd(&p.counters[kh], 1u) == SPLITS - 1) ? 1 : 0;
     bar_sync(bar_id, kAttnThreads);
     if (sh->last) {
         __threadfence();
         // Merge the splits in parallel: (max, sum) of every (split, head) pair to shared memory,
         // one rescale weight per pair, then thread d sums its dimension over the splits.
-        const float* base = p.part + static_cast<size_t>(kh * kAttnSplits) * group * (hd + 2);
+        const float* base = p.part + static_cast<size_t>(kh * SPLITS) * group * (hd + 2);
         float gate[kAttnMaxGroup];  // output gates, loaded with the (max, sum) pairs
 #pragma unroll
         for (int g = 0; g < kAttnMaxGroup; ++g)
             gate[g] = g < group ? __ldcg(p.qkv + static_cast<size_t>(kh * group + g) * 2 * hd + hd + tid) : 0.0f;
-        if (tid < kAttnSplits * group) {
+        if (tid < SPLITS * group) {
             const float* ps = base + tid * (hd + 2);  // tid = split * group + g
             sh->pm[tid] = __ldcg(ps + hd);
             sh->pl[tid] = __ldcg(ps + hd + 1);
@@ -305,24 +305,24 @@ __device__ __forceinline__ void attention_item(const AttnParams& p, int kh, int 
         bar_sync(bar_id, kAttnThreads);
         if (tid < group) {
             float M = -INFINITY;
-            for (int s2 = 0; s2 < kAttnSplits; ++s2) M = fmaxf(M, sh->pm[s2 * group + tid]);
+            for (int s2 = 0; s2 < SPLITS; ++s2) M = fmaxf(M, sh->pm[s2 * group + tid]);
             float Ls = 0.0f;
-            for (int s2 = 0; s2 < kAttnSplits; ++s2) Ls += sh->pl[s2 * group + tid] * expf(sh->pm[s2 * group + tid] - M);
+            for (int s2 = 0; s2 < SPLITS; ++s2) Ls += sh->pl[s2 * group + tid] * expf(sh->pm[s2 * group + tid] - M);
             sh->M[tid] = M;
             sh->invL[tid] = Ls > 0.0f ? 1.0f / Ls : 0.0f;
         }
         bar_sync(bar_id, kAttnThreads);
-        if (tid < kAttnSplits * group) sh->pm[tid] = expf(sh->pm[tid] - sh->M[tid % group]);
+        if (tid < SPLITS * group) sh->pm[tid] = expf(sh->pm[tid] - sh->M[tid % group]);
         bar_sync(bar_id, kAttnThreads);
 #pragma unroll
         for (int g = 0; g < kAttnMaxGroup; ++g) {
             if (g >= group) break;
-            float part[kAttnSplits];  // every split of this head in flight in one round trip
+            float part[SPLITS];  // every split of this head in flight in one round trip
 #pragma unroll
-            for (int u = 0; u < kAttnSplits; ++u) part[u] = __ldcg(base + (u * group + g) * (hd + 2) + tid);
+            for (int u = 0; u < SPLITS; ++u) part[u] = __ldcg(base + (u * group + g) * (hd + 2) + tid);
             float O = 0.0f;
 #pragma unroll
-            for (int u = 0; u < kAttnSplits; ++u) O += part[u] * sh->pm[u * group + g];
+            for (int u = 0; u < SPLITS; ++u) O += part[u] * sh->pm[u * group + g];
             const int qh = kh * group + g;
             const float val = (O * sh->invL[g]) * dsigmoid(gate[g]);  // output gate, custom_model.cpp:944-946
             if (out_hi) {  // batched decode: the o_proj GEMM operands as a bf16 pair
