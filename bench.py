@@ -433,10 +433,10 @@ def config4_batched(pkg, model_dir, peak_gbs, weight_bytes, batches=(1, 8, 64), 
             "points": out}
 
 
-def cpu_baseline(model_dir, steps, preset="cfg2", prompt=PROMPT_LEN):
+def cpu_baseline(model_dir, steps, preset="cfg2", prompt=PROMPT_LEN, warmup=0):
     """The reference's own CPU path (compiled from its sources) on the same package and context,
-    on a bounded sample: a `prompt`-token prefill (untimed), then `steps` greedy decode tokens
-    through its C ABI, timed."""
+    on a bounded sample: a `prompt`-token prefill and `warmup` decode tokens (untimed), then
+    `steps` greedy decode tokens through its C ABI, timed."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
@@ -450,14 +450,17 @@ def cpu_baseline(model_dir, steps, preset="cfg2", prompt=PROMPT_LEN):
         s = oracle.PortModel(model_dir)
         kind = "port"
     s.prefill(ids)
+    for _ in range(warmup):
+        s.decode_one()
     t = time.time()
     for _ in range(steps):
         s.decode_one()
     dt = time.time() - t
     s.close()
     return dict({"value": round(steps / dt, 4), "unit": "tok/s", "cores": cores, "kind": kind,
-                 "sample": f"{steps} greedy decode steps after a {prompt}-token prompt (context {prompt}.."
-                           f"{prompt + steps}) on the {'9B' if preset == 'cfg2' else preset} package; the "
+                 "sample": f"{steps} greedy decode steps after a {prompt}-token prompt and {warmup} untimed "
+                           f"steps (context {prompt + warmup}..{prompt + warmup + steps}) on the "
+                           f"{'9B' if preset == 'cfg2' else preset} package; the "
                            f"reference's WorkerPool caps at min(8, hardware_concurrency) threads"}, **host_cpu())
 
 
@@ -485,12 +488,12 @@ def run_reference_arm(args, rank, world):
     __graft_entry__.load_package()  # registers the package module for the synthetic data generator
     d = make_package(0, 1, args.preset)
     steps = max(1, min(args.steps, 16))
-    warm = 0  # the untimed 512-token prefill warms the reference's caches and thread pool
+    warm = max(0, min(args.warmup, 3))  # untimed decode steps after the prompt (~1 s each on the host)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
 
     prompt = min(args.prompt, PROMPT_LEN)
-    cb = cpu_baseline(d, steps, args.preset, prompt=prompt)
+    cb = cpu_baseline(d, steps, args.preset, prompt=prompt, warmup=warm)
     line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": steps, "warmup": warm, "ms_per_step": round(1000.0 / cb["value"], 2) if cb["value"] else None,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
